@@ -1,0 +1,472 @@
+"""Benchmark of the fused W4A16 GEMM (the reference's headline metric).
+
+Metric: effective TFLOP/s (2*M*N*K / time) at M=N=K=4096 for
+group 32, 64 and 128; decode-shaped HBM GB/s; fraction of peak.
+
+A step is the headline workload of configs[1]: three fused GEMMs at
+M=N=K=4096, one per group size (32, 64, 128), each on its own quantised
+weight, FP16 C. Under torchrun every rank owns its own 4096-column slice of
+a column-parallel weight (N_total = 4096 * world), so per-GPU work is fixed
+("weak" scaling) and no collective is on the data path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+The reference arm (--impl reference) times the reference's own CPU
+implementation of the path (oracle/_ref: its unmodified src/reference.cu,
+dequantize_cpu + cpu_gemm_fp32, one std::thread per host core over disjoint
+row slices) on a bounded row sample of the same workload, extrapolated.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+M_HEAD = N_HEAD = K_HEAD = 4096
+GROUPS = (32, 64, 128)
+METRIC = "Effective TFLOP/s @4096^3 g32/64/128"
+UNIT = "TFLOP/s"
+WORKLOAD = "fused W4A16 GEMM, M=N=K=4096, groups 32/64/128 (one GEMM each per step)"
+
+
+def flops(M, N, K):
+    return 2.0 * M * N * K
+
+
+def algorithmic_bytes(M, N, K, g):
+    return 2 * M * K + K * N // 2 + 2 * N * (K // g) + 2 * M * N
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+def load_profile_traffic():
+    """dram bytes per launch from the committed ncu summary, if present."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f)
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.proc = None
+        self.lines = []
+        self.first = 0
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 5.0:
+                time.sleep(0.01)
+            self.first = len(self.lines)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        return False
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines[max(0, self.first - 1):]:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------ our arm
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    import sm_120__gemm_b200 as i4g
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    stream = torch.cuda.current_stream()
+    M, K = M_HEAD, K_HEAD
+    n_local = N_HEAD
+    n_total = n_local * world
+    peaks = load_peaks()
+
+    # Seeded synthetic inputs: A fp16 U[-1,1]; W fp32 N(0, 0.02) -> fp16 ->
+    # quantised on the GPU (codes bit-identical to quantize_cpu). Each rank
+    # builds only its own column slice of the full weight (seeded by rank).
+    def weights(g, rep):
+        gen = torch.Generator(device=dev).manual_seed(5678 + 1000 * rep + 17 * g + 7919 * rank)
+        w = (torch.randn(K, n_local, generator=gen, device=dev) * 0.02).half()
+        return i4g.QuantizedLinear.from_weight(w, g)
+
+    # Rotating inputs keep each GEMM's operands out of L2 (126 MB) when the
+    # GEMM runs: 4 activation buffers (32 MiB each) and 2 weight sets per group.
+    n_act, n_wset = 4, 2
+    gen_a = torch.Generator(device=dev).manual_seed(1234 + rank)
+    acts = [(torch.rand(M, K, generator=gen_a, device=dev) * 2 - 1).half() for _ in range(n_act)]
+    lins = {g: [weights(g, r) for r in range(n_wset)] for g in GROUPS}
+    outs = [torch.empty(M, n_local, dtype=torch.float16, device=dev) for _ in range(3)]
+    torch.cuda.synchronize()
+
+    def step(i, events=None):
+        for j, g in enumerate(GROUPS):
+            lin = lins[g][(i + j) % n_wset]
+            a = acts[(3 * i + j) % n_act]
+            if events is not None:
+                events[j][0].record(stream)
+            i4g.launch_final(a, lin.tiles, lin.scales, outs[j], M, n_local, K, g, stream)
+            if events is not None:
+                events[j][1].record(stream)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if i4g.device_status() != 0:
+        raise RuntimeError("device-side wait timed out during warm-up")
+
+    kernel_events = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in GROUPS]
+                     for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clocks:
+        start.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i, kernel_events[i])
+        stop.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(stop)
+    per_group_ms = {g: [kernel_events[i][j][0].elapsed_time(kernel_events[i][j][1])
+                        for i in range(args.steps)] for j, g in enumerate(GROUPS)}
+    if i4g.device_status() != 0:
+        raise RuntimeError("device-side wait timed out during timing")
+
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+
+    step_flops_rank = sum(flops(M, n_local, K) for _ in GROUPS)
+    value = step_flops_rank * world * args.steps / (ms_max * 1e-3) / 1e12
+    kernel_ms = {g: statistics.mean(v) for g, v in per_group_ms.items()}
+    kernel_total_ms = sum(kernel_ms.values())
+    achieved = step_flops_rank / (kernel_total_ms * 1e-3) / 1e12
+    result = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded): A fp16 U[-1,1]; W fp32 N(0,0.02) -> fp16 -> INT4",
+        "config": {"workload": WORKLOAD, "M": M, "N_per_gpu": n_local, "N_total": n_total,
+                   "K": K, "groups": list(GROUPS), "parallelism": f"column-parallel x{world}",
+                   "l2": "rotating inputs: 4 x 32 MiB activations, 2 weight sets per group"},
+        "per_group": {str(g): {"kernel_ms": round(kernel_ms[g], 4),
+                               "tflops": round(flops(M, n_local, K) / kernel_ms[g] / 1e9, 1)}
+                      for g in GROUPS},
+        "gpu_launches": args.steps * len(GROUPS),
+    }
+    traffic = load_profile_traffic().get("tc_4096_g128_bytes_per_launch")
+    result["roofline"] = {
+        "bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"],
+        "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
+        "traffic": traffic,
+        "peak_source": f"{peaks['source']} (cuBLAS bf16 burst; fp16 dense runs at the bf16 rate)",
+        "kernel": "gemm_tc_kernel (tcgen05, TMEM)",
+        "algorithmic_bytes_per_launch": algorithmic_bytes(M, n_local, K, 128),
+    }
+    result["clocks"] = clocks.summary()
+
+    if rank == 0 and world == 1 and not args.no_extras:
+        result["e2e"] = run_e2e(args, i4g, lins, dev)
+        result["decode"] = run_decode(args, i4g, dev, peaks)
+        result["cpu_baseline"] = cpu_baseline(args, sample_rows=args.cpu_rows)
+    elif rank == 0:
+        result["e2e"] = run_e2e(args, i4g, lins, dev)
+    return result
+
+
+def run_e2e(args, i4g, lins, dev):
+    """Same metric through the public API with host buffers: every GEMM copies
+    its A from pinned host memory and reads its C back, inside the timed loop."""
+    import torch
+
+    M, K, N = M_HEAD, K_HEAD, N_HEAD
+    stream = torch.cuda.current_stream()
+    a_host = [(torch.rand(M, K, generator=torch.Generator().manual_seed(99 + j)) * 2 - 1)
+              .half().pin_memory() for j in range(len(GROUPS))]
+    c_host = [torch.empty(M, N, dtype=torch.float16).pin_memory() for _ in GROUPS]
+    a_dev = torch.empty(M, K, dtype=torch.float16, device=dev)
+    c_dev = torch.empty(M, N, dtype=torch.float16, device=dev)
+
+    def step():
+        for j, g in enumerate(GROUPS):
+            a_dev.copy_(a_host[j], non_blocking=True)
+            lins[g][0](a_dev, out=c_dev)
+            c_host[j].copy_(c_dev, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    steps = max(3, args.steps // 2)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        step()
+    stop.record(stream)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(stop) / steps
+    return {"value": round(sum(flops(M, N, K) for _ in GROUPS) / (ms * 1e-3) / 1e12, 2),
+            "unit": UNIT, "h2d_bytes_per_step": len(GROUPS) * M * K * 2,
+            "d2h_bytes_per_step": len(GROUPS) * M * N * 2, "ms_per_step": round(ms, 4),
+            "path": "QuantizedLinear -> launch_final (C ABI i4g_gemm), pinned host A and C"}
+
+
+def run_decode(args, i4g, dev, peaks):
+    """Decode-shaped HBM GB/s: M in {1,4,8,16}, g128, both MLP
+    shapes, rotating weight sets whose total exceeds L2 (cold weights)."""
+    import torch
+
+    stream = torch.cuda.current_stream()
+    out = {}
+    for (K, N) in ((4096, 14336), (14336, 4096)):
+        nsets = 6  # 6 x ~30 MB > 126 MB L2
+        gen = torch.Generator(device=dev).manual_seed(4242 + K)
+        lins = []
+        for _ in range(nsets):
+            w = (torch.randn(K, N, generator=gen, device=dev) * 0.02).half()
+            lins.append(i4g.QuantizedLinear.from_weight(w, 128))
+            del w
+        for M in (1, 4, 8, 16):
+            a = torch.randn(M, K, generator=gen, device=dev).half()
+            c = torch.empty(M, N, dtype=torch.float16, device=dev)
+            iters = 120
+            for i in range(nsets):
+                lins[i % nsets](a, out=c)
+            torch.cuda.synchronize()
+            # Back-to-back launches captured in one CUDA graph, so the host's
+            # per-call cost is not in the device time.
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(side):
+                with torch.cuda.graph(graph, stream=side):
+                    for i in range(iters):
+                        lins[i % nsets](a, out=c, stream=side)
+            torch.cuda.current_stream().wait_stream(side)
+            graph.replay()
+            torch.cuda.synchronize()
+            start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+            graph.replay()
+            stop.record(stream)
+            torch.cuda.synchronize()
+            del graph
+            us = start.elapsed_time(stop) * 1e3 / iters
+            nbytes = algorithmic_bytes(M, N, K, 128)
+            gbs = nbytes / (us * 1e-6) / 1e9
+            out[f"M{M}_K{K}_N{N}"] = {"us": round(us, 2), "hbm_gbs": round(gbs, 1),
+                                     "frac_hbm": round(gbs / peaks["hbm_gbs"], 3)}
+        del lins
+        torch.cuda.empty_cache()
+    return out
+
+
+# ------------------------------------------------------- CPU reference arm
+
+def _cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+_CPU_CASES = {}
+
+
+def _cpu_case(group):
+    """Quantised 4096x4096 weight of the CPU arm (built once per group)."""
+    import numpy as np
+
+    import oracle
+
+    if group not in _CPU_CASES:
+        K, N = K_HEAD, N_HEAD
+        rng = np.random.default_rng(5678 + group)
+        w = oracle.f2h(rng.standard_normal((K, N)).astype(np.float32) * np.float32(0.02))
+        _CPU_CASES[group] = oracle.quantize(w, K, N, group)  # bit-identical to quantize_cpu
+    return _CPU_CASES[group]
+
+
+def cpu_sample(rows, threads, group=128, seed=0):
+    """Time the reference's CPU path (oracle/_ref if built, else the oracle
+    port) on `rows` rows of the 4096^3 workload: dequantize_cpu of the whole
+    weight, then cpu_gemm_fp32 on the row sample. Returns seconds and kind."""
+    import numpy as np
+
+    import oracle
+
+    N, K = N_HEAD, K_HEAD
+    rng = np.random.default_rng(seed)
+    a = oracle.f2h(rng.uniform(-1, 1, (rows, K)).astype(np.float32))
+    packed, scales = _cpu_case(group)
+    if oracle.ref_available():
+        kind = "reference"
+        t0 = time.perf_counter()
+        deq = oracle.ref_dequantize(packed, scales, K, N, group)
+        t1 = time.perf_counter()
+        oracle.ref_gemm_rows(a, deq, rows, N, K, threads=threads)
+        t2 = time.perf_counter()
+    else:
+        kind = "port"
+        t0 = time.perf_counter()
+        deq = oracle.dequantize(packed, scales, K, N, group)
+        t1 = time.perf_counter()
+        oracle.gemm_rows(a, deq, rows, N, K, threads=threads)
+        t2 = time.perf_counter()
+    return t1 - t0, t2 - t1, kind
+
+
+def cpu_baseline(args, sample_rows):
+    threads = _cpu_threads()
+    rows = max(sample_rows, threads)
+    t_deq, t_rows, kind = cpu_sample(rows, threads)
+    t_full = t_deq + t_rows * (M_HEAD / rows)
+    value = flops(M_HEAD, N_HEAD, K_HEAD) / t_full / 1e12
+    return {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
+            "sample": f"dequantize_cpu of the 4096x4096 g128 weight + cpu_gemm_fp32 on {rows} "
+                      f"of 4096 rows ({threads} threads), extrapolated to the full GEMM",
+            "seconds_measured": round(t_deq + t_rows, 3)}
+
+
+def run_reference(args):
+    """Each step times the reference's CPU path on one bounded sample (one
+    group per step, cycling 32/64/128: the full dequantize_cpu plus
+    cpu_gemm_fp32 on a row sample); a 3-GEMM step's time is the sum of the
+    per-group extrapolated times, averaged over the steps."""
+    threads = _cpu_threads()
+    rows = max(args.cpu_rows // 2, threads)
+    for i in range(args.warmup):
+        cpu_sample(threads, threads, group=GROUPS[i % len(GROUPS)], seed=100 + i)
+    per_group = {g: [] for g in GROUPS}
+    kind = "port"
+    for i in range(args.steps):
+        g = GROUPS[i % len(GROUPS)]
+        t_deq, t_rows, kind = cpu_sample(rows, threads, group=g, seed=i)
+        per_group[g].append(t_deq + t_rows * (M_HEAD / rows))
+    ms_step = 1e3 * sum(statistics.mean(v) for v in per_group.values() if v) * (
+        len(GROUPS) / max(1, sum(1 for v in per_group.values() if v)))
+    value = sum(flops(M_HEAD, N_HEAD, K_HEAD) for _ in GROUPS) / (ms_step * 1e-3) / 1e12
+    sample = (f"per step: one group's dequantize_cpu of the 4096x4096 weight + cpu_gemm_fp32 "
+              f"on {rows} of 4096 rows ({threads} threads), extrapolated to the full GEMM; "
+              f"groups cycle 32/64/128")
+    return {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 2), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "impl": "reference",
+        "data": "synthetic (seeded): A fp16 U[-1,1]; W fp32 N(0,0.02) -> fp16 -> INT4",
+        "config": {"workload": WORKLOAD, "M": M_HEAD, "N_per_gpu": N_HEAD, "K": K_HEAD,
+                   "groups": list(GROUPS), "parallelism": "host threads"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-rows", type=int, default=64)
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the e2e / decode / cpu-baseline legs")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args)), flush=True)
+        return
+
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        result = run_ours(args, rank, world, local_rank)
+        if rank == 0:
+            print(json.dumps(result), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,160 @@
+/*
+ * i4g: B200-native (sm_100a) fused W4A16 INT4 weight-only GEMM, C ABI.
+ *
+ *   C[M,N] = A_fp16[M,K] x dequant(B_int4[K,N], fp16 group scale),
+ *   FP32 accumulation, FP16 (or FP32) output, group size 32 / 64 / 128.
+ *
+ * This is the drop-in boundary for the hot path of zichaowen8-prog/SM_120__GEMM.
+ * Each entry point replaces one host function of the reference's C++ API
+ * (cited beside it); the C++ wrappers with the reference's exact signatures
+ * are in int4gemm.hpp.
+ *
+ * Conventions
+ *   - Pointers are caller-owned device memory; no entry point allocates
+ *     device memory. `half` data is passed as void* (IEEE binary16).
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream). Work is
+ *     stream-ordered; no entry point synchronises the host.
+ *   - Return 0 (I4G_OK) or a negative i4g_status. Shapes, group and
+ *     alignment are checked before anything is launched.
+ *   - Layouts: A is row-major [M][K]; C row-major [M][N]; `packed` is the
+ *     reference's row-major nibble stream (element k*N+n, even element in the
+ *     low nibble, src/quantize.cu:25-39); `scales` is [ceil(K/g)][N].
+ *     The GEMM consumes the "tile" weight layout written by i4g_repack_umma
+ *     (blocks of 128 columns x 64 k) and the scale layout written by
+ *     i4g_repack_scales_128 ([N/128][K/g][128], include/layout.cuh:27-32).
+ */
+#ifndef I4G_H
+#define I4G_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  I4G_OK = 0,
+  I4G_ERR_NULL_POINTER = -1,   /* a required pointer is NULL */
+  I4G_ERR_SHAPE = -2,          /* M/N/K out of range or not a tile multiple */
+  I4G_ERR_GROUP = -3,          /* group size not 32, 64 or 128, or K % group */
+  I4G_ERR_ALIGNMENT = -4,      /* pointer not aligned as the layout needs */
+  I4G_ERR_CUDA = -5,           /* a CUDA runtime call failed */
+  I4G_ERR_DRIVER = -6,         /* tensor-map encoding failed */
+  I4G_ERR_DEVICE = -7,         /* current device is not sm_100 */
+  I4G_ERR_TIMEOUT = -8,        /* a device-side wait hit its limit */
+  I4G_ERR_VARIANT = -9         /* unknown kernel variant */
+} i4g_status;
+
+/* Kernel selection for i4g_gemm_variant. */
+typedef enum {
+  I4G_VARIANT_AUTO = 0,        /* the dispatch i4g_gemm uses */
+  I4G_VARIANT_TC = 1,          /* tcgen05 + TMEM warp-specialised kernel */
+  I4G_VARIANT_DECODE = 2       /* tensor-core GEMV-style kernel, M <= 16 */
+} i4g_variant;
+
+/* Human-readable text for a status code (static storage). */
+const char* i4g_status_string(int status);
+/* Text of the last CUDA / driver error seen on this host thread. */
+const char* i4g_last_error(void);
+/* Version of the tile layout written by i4g_repack_umma. */
+int i4g_layout_version(void);
+
+/* ---- preprocessing (include/quant.cuh:6-21) ------------------------------ */
+
+/* launch_quantize (include/quant.cuh:6-7, src/quantize.cu:54-62).
+ * Codes and scales are bit-identical to quantize_cpu (src/reference.cu:6-26).
+ * K % group may be non-zero (the last group is partial), as in the reference.
+ * N must be even. */
+int i4g_quantize(const void* b, uint8_t* packed, void* scales,
+                 int K, int N, int group, void* stream);
+
+/* launch_dequantize (include/quant.cuh:8-9, src/quantize.cu:64-69):
+ * b[k][n] = half(q * scale), bit-identical to dequantize_cpu. */
+int i4g_dequantize(const uint8_t* packed, const void* scales, void* b,
+                   int K, int N, int group, void* stream);
+
+/* launch_repack_128x32 (include/quant.cuh:10-12, src/repack.cu:124-135):
+ * tile-contiguous nibbles [N/128][K/32][32][128] plus the 128-column scale
+ * layout. K % 32 == 0, N % 128 == 0, K % group == 0. */
+int i4g_repack_128x32(const uint8_t* packed, const void* scales,
+                      uint8_t* repacked, void* repacked_scales,
+                      int K, int N, int group, void* stream);
+
+/* launch_inverse_repack_128x32 (include/quant.cuh:13-14, src/repack.cu:137-142). */
+int i4g_inverse_repack_128x32(const uint8_t* repacked, uint8_t* packed,
+                              int K, int N, void* stream);
+
+/* launch_repack_mma_128x32 (include/quant.cuh:15-16, src/repack.cu:144-152):
+ * the reference's mma.sync lane-native B-fragment words. */
+int i4g_repack_mma_128x32(const uint8_t* packed, uint8_t* repacked,
+                          int K, int N, void* stream);
+
+/* launch_repack_mma_pair_128x32 (include/quant.cuh:17-18, src/repack.cu:154-162). */
+int i4g_repack_mma_pair_128x32(const uint8_t* packed, uint8_t* repacked,
+                               int K, int N, void* stream);
+
+/* launch_repack_scales_128 (include/quant.cuh:19-21, src/repack.cu:164-174):
+ * [K/g][N] -> [N/128][K/g][128]. This is also the GEMM's scale layout. */
+int i4g_repack_scales_128(const void* scales, void* repacked_scales,
+                          int K, int N, int group, void* stream);
+
+/* New layout for the sm_100a kernels (replaces the lane-native repacks that
+ * launch_final consumes, src/main.cu:322-329). Blocks of 128 columns x 64 k,
+ * ordered [N/128][K/64], 4096 bytes each; inside a block
+ * [h = (k%64)/32][n%128][w = (k%32)/8] uint32 words, and in a word element
+ * k%8 = 2p + hi at bit 4p + 16hi. An N-slice at a multiple of 128 columns is
+ * one contiguous byte range. K % 64 == 0, N % 128 == 0. */
+int i4g_repack_umma(const uint8_t* packed, uint8_t* tiles,
+                    int K, int N, void* stream);
+/* Inverse of i4g_repack_umma (test and serialisation aid). */
+int i4g_inverse_repack_umma(const uint8_t* tiles, uint8_t* packed,
+                            int K, int N, void* stream);
+
+/* ---- fused GEMM (include/kernels.cuh:24-25, 81-83) ------------------------ */
+
+/* launch_final (kernels/gemm_final.cu:5-13): C fp16 [M][N] = A x dequant(B).
+ * tiles: i4g_repack_umma output; scales: i4g_repack_scales_128 output.
+ * Any M >= 1; N % 128 == 0; K % 64 == 0; K % group == 0; group in {32,64,128}
+ * (other groups are rejected, where the reference silently ran g128).
+ * Dispatch: M <= 16 uses the decode kernel, larger M the tcgen05 kernel. */
+int i4g_gemm(const void* A, const uint8_t* tiles, const void* scales, void* C,
+             int M, int N, int K, int group, void* stream);
+
+/* launch_final_fp32 (include/kernels.cuh:81, kernels/gemm_v09_async.cu:61):
+ * the same product with an FP32 C (tcgen05 kernel, FP32 epilogue). */
+int i4g_gemm_fp32(const void* A, const uint8_t* tiles, const void* scales,
+                  float* C, int M, int N, int K, int group, void* stream);
+
+/* i4g_gemm with an explicit kernel choice (tests and benchmarks). */
+int i4g_gemm_variant(const void* A, const uint8_t* tiles, const void* scales,
+                     void* C, int M, int N, int K, int group, int variant,
+                     void* stream);
+
+/* ---- column-parallel sharding --------------------------------------------- */
+
+/* Byte offsets of rank `rank`'s slice of a G-way column-parallel split of the
+ * tile layout and the scale layout, and its columns [*n0, *n1). N / G must
+ * be a multiple of 128. The slices are contiguous, so a rank's weights are
+ * (tiles + *tile_offset, scales + *scale_offset) with N_local = *n1 - *n0. */
+int i4g_shard_range(int K, int N, int group, int world, int rank,
+                    size_t* tile_offset, size_t* scale_offset,
+                    int* n0, int* n1);
+
+/* ---- device status --------------------------------------------------------- */
+
+/* Reads and clears this device's kernel status word (set when a device-side
+ * wait hits its limit). Synchronises `stream`. *out = 0 when clean. */
+int i4g_device_status(int* out, void* stream);
+
+/* Diagnostic: launches a one-warp kernel whose mbarrier wait can never
+ * complete, through the same bounded wait the GEMM kernels use. It gives up
+ * after limit_ns (at most 1 s) and records I4G_ERR_TIMEOUT in the device
+ * status word, without faulting the GPU. */
+int i4g_selftest_wait_timeout(unsigned long long limit_ns, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* I4G_H */

@@ -1,0 +1,442 @@
+// The C ABI of include/i4g.h: argument checks, device checks, tensor maps
+// and dispatch to the kernels. Nothing here allocates device memory.
+#include "../../include/i4g.h"
+#include "gemm_tc.h"
+#include "ptx.cuh"
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+namespace {
+
+// Per-device kernel status word: a bounded device-side wait that gives up
+// records I4G_ERR_TIMEOUT here (see ptx.cuh, mbar_wait).
+__device__ int g_status_word;
+
+constexpr int kMaxDevices = 64;
+constexpr unsigned long long kDefaultWaitLimitNs = 2000000000ull;  // 2 s
+
+thread_local char t_last_error[512] = "";
+
+struct DeviceInfo {
+  bool ready = false;
+  int status = I4G_OK;  // I4G_OK or I4G_ERR_DEVICE
+  int sm_count = 0;
+  int* status_word = nullptr;
+};
+DeviceInfo g_devices[kMaxDevices];
+std::mutex g_device_mutex;
+
+int record_cuda(cudaError_t e, const char* what) {
+  std::snprintf(t_last_error, sizeof(t_last_error), "%s: %s (%s)", what, cudaGetErrorName(e),
+                cudaGetErrorString(e));
+  return I4G_ERR_CUDA;
+}
+
+// Checks the current device once (compute capability 10.0, the sm_100a
+// target this library is built for) and caches its SM count and the device
+// address of its status word.
+int current_device(DeviceInfo** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return record_cuda(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) {
+    std::snprintf(t_last_error, sizeof(t_last_error), "device ordinal %d out of range", dev);
+    return I4G_ERR_DEVICE;
+  }
+  DeviceInfo& info = g_devices[dev];
+  std::lock_guard<std::mutex> lock(g_device_mutex);
+  if (!info.ready) {
+    int major = 0, minor = 0, sms = 0;
+    if ((e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+      return record_cuda(e, "cudaDeviceGetAttribute");
+    if (major != 10 || minor != 0) {
+      std::snprintf(t_last_error, sizeof(t_last_error),
+                    "device %d is sm_%d%d; this library is built for sm_100a only", dev, major,
+                    minor);
+      info.status = I4G_ERR_DEVICE;
+    } else {
+      void* p = nullptr;
+      if ((e = cudaGetSymbolAddress(&p, g_status_word)) != cudaSuccess)
+        return record_cuda(e, "cudaGetSymbolAddress(status word)");
+      info.status_word = static_cast<int*>(p);
+      info.sm_count = sms;
+      info.status = I4G_OK;
+    }
+    info.ready = true;
+  }
+  if (info.status != I4G_OK) return info.status;
+  *out = &info;
+  return I4G_OK;
+}
+
+int fail(int code, const char* fmt, int a = 0, int b = 0, int c = 0) {
+  std::snprintf(t_last_error, sizeof(t_last_error), fmt, a, b, c);
+  return code;
+}
+
+bool aligned(const void* p, size_t bytes) {
+  return (reinterpret_cast<uintptr_t>(p) % bytes) == 0;
+}
+
+int check_group(int K, int group, bool require_divisible) {
+  if (group != 32 && group != 64 && group != 128)
+    return fail(I4G_ERR_GROUP, "group %d is not 32, 64 or 128", group);
+  if (require_divisible && K % group != 0)
+    return fail(I4G_ERR_GROUP, "K=%d is not a multiple of group %d", K, group);
+  return I4G_OK;
+}
+
+int finish(cudaError_t e, const char* what) {
+  return e == cudaSuccess ? I4G_OK : record_cuda(e, what);
+}
+
+// ---------------------------------------------------------- tensor maps
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int encode_fn(EncodeTiledFn* out) {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (err == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  if (!fn) {
+    if (err != cudaSuccess) return record_cuda(err, "cudaGetDriverEntryPoint");
+    return fail(I4G_ERR_DRIVER, "cuTensorMapEncodeTiled is unavailable");
+  }
+  *out = fn;
+  return I4G_OK;
+}
+
+// Activation map: A [M][K] fp16, box 64 (K) x tile_m (M) rows, 128-byte
+// swizzle, zero fill past M. Cached per host thread and key, as the
+// reference caches its maps (kernels/gemm_v17_instruction.cu:214-228).
+struct ActMapCache {
+  int device = -1;
+  const void* a = nullptr;
+  int M = 0, K = 0, tile_m = 0;
+  CUtensorMap map;
+};
+
+int act_map(const void* A, int M, int K, int tile_m, const CUtensorMap** out) {
+  thread_local ActMapCache cache;
+  int dev = -1;
+  cudaGetDevice(&dev);
+  if (cache.device == dev && cache.a == A && cache.M == M && cache.K == K &&
+      cache.tile_m == tile_m) {
+    *out = &cache.map;
+    return I4G_OK;
+  }
+  EncodeTiledFn encode = nullptr;
+  int st = encode_fn(&encode);
+  if (st != I4G_OK) return st;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
+  const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(tile_m)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = encode(&cache.map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(A),
+                            dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    cache.device = -1;
+    return fail(I4G_ERR_DRIVER, "cuTensorMapEncodeTiled failed with CUresult %d", int(r));
+  }
+  cache.device = dev;
+  cache.a = A;
+  cache.M = M;
+  cache.K = K;
+  cache.tile_m = tile_m;
+  *out = &cache.map;
+  return I4G_OK;
+}
+
+unsigned long long g_wait_limit_ns = kDefaultWaitLimitNs;
+
+int gemm_common(const void* A, const uint8_t* tiles, const void* scales, void* C, bool fp32_out,
+                int M, int N, int K, int group, int variant, void* stream) {
+  if (!A || !tiles || !scales || !C) return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
+  if (M < 1 || N < 128 || K < 64 || N % 128 != 0 || K % 64 != 0)
+    return fail(I4G_ERR_SHAPE,
+                "shape M=%d N=%d K=%d: need M >= 1, N %% 128 == 0, K %% 64 == 0", M, N, K);
+  if (static_cast<long long>(M) * K >= (1ll << 40) || static_cast<long long>(M) * N >= (1ll << 40))
+    return fail(I4G_ERR_SHAPE, "shape M=%d N=%d K=%d too large", M, N, K);
+  int st = check_group(K, group, true);
+  if (st != I4G_OK) return st;
+  if (!aligned(A, 16) || !aligned(tiles, 16) || !aligned(scales, 16) ||
+      !aligned(C, fp32_out ? 4 : 2))
+    return fail(I4G_ERR_ALIGNMENT, "A, tiles and scales must be 16-byte aligned");
+  if (variant != I4G_VARIANT_AUTO && variant != I4G_VARIANT_TC && variant != I4G_VARIANT_DECODE)
+    return fail(I4G_ERR_VARIANT, "unknown variant %d", variant);
+  if (variant == I4G_VARIANT_AUTO)
+    variant = (!fp32_out && M <= i4g::dec::MAX_M) ? I4G_VARIANT_DECODE : I4G_VARIANT_TC;
+  if (variant == I4G_VARIANT_DECODE && (fp32_out || M > i4g::dec::MAX_M))
+    return fail(I4G_ERR_VARIANT, "decode variant needs M <= %d and an FP16 C (M=%d)",
+                i4g::dec::MAX_M, M);
+  DeviceInfo* dev = nullptr;
+  st = current_device(&dev);
+  if (st != I4G_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const __half* sc = static_cast<const __half*>(scales);
+  if (variant == I4G_VARIANT_DECODE)
+    return finish(i4g::dec::launch(static_cast<const __half*>(A), tiles, sc,
+                                   static_cast<__half*>(C), M, N, K, group, s),
+                  "decode kernel launch");
+  const int tile_m = i4g::tc::choose_tile_m(M, N, dev->sm_count);
+  const CUtensorMap* map = nullptr;
+  st = act_map(A, M, K, tile_m, &map);
+  if (st != I4G_OK) return st;
+  return finish(i4g::tc::launch(*map, tile_m, tiles, sc, C, fp32_out, M, N, K, group,
+                                dev->sm_count, dev->status_word, g_wait_limit_ns, s),
+                "tcgen05 kernel launch");
+}
+
+// A kernel that waits on an mbarrier nothing will complete, through the same
+// bounded wait the GEMM kernels use; it must give up and report a timeout.
+__global__ void wait_timeout_selftest_kernel(int* status, unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    i4g::mbar_init(i4g::smem_u32(&bar), 1);
+    abort_flag = 0;
+    i4g::fence_mbarrier_init();
+  }
+  __syncthreads();
+  i4g::mbar_wait(i4g::smem_u32(&bar), 0, reinterpret_cast<volatile int*>(&abort_flag), status,
+                 limit_ns);
+  __syncthreads();
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* i4g_status_string(int status) {
+  switch (status) {
+    case I4G_OK: return "ok";
+    case I4G_ERR_NULL_POINTER: return "null pointer argument";
+    case I4G_ERR_SHAPE: return "unsupported shape";
+    case I4G_ERR_GROUP: return "unsupported group size";
+    case I4G_ERR_ALIGNMENT: return "misaligned pointer";
+    case I4G_ERR_CUDA: return "CUDA runtime error";
+    case I4G_ERR_DRIVER: return "CUDA driver (tensor map) error";
+    case I4G_ERR_DEVICE: return "unsupported device (needs sm_100)";
+    case I4G_ERR_TIMEOUT: return "device-side wait timed out";
+    case I4G_ERR_VARIANT: return "unsupported kernel variant";
+    default: return "unknown status";
+  }
+}
+
+const char* i4g_last_error(void) { return t_last_error; }
+
+int i4g_layout_version(void) { return 1; }
+
+int i4g_quantize(const void* b, uint8_t* packed, void* scales, int K, int N, int group,
+                 void* stream) {
+  if (!b || !packed || !scales) return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
+  if (K < 1 || N < 2 || N % 2 != 0)
+    return fail(I4G_ERR_SHAPE, "quantize needs K >= 1 and an even N (K=%d N=%d)", K, N);
+  int st = check_group(K, group, false);
+  if (st != I4G_OK) return st;
+  if (!aligned(b, 4) || !aligned(scales, 2))
+    return fail(I4G_ERR_ALIGNMENT, "b must be 4-byte aligned");
+  DeviceInfo* dev = nullptr;
+  if ((st = current_device(&dev)) != I4G_OK) return st;
+  return finish(i4g::prep::quantize(static_cast<const __half*>(b), packed,
+                                    static_cast<__half*>(scales), K, N, group,
+                                    static_cast<cudaStream_t>(stream)),
+                "quantize launch");
+}
+
+int i4g_dequantize(const uint8_t* packed, const void* scales, void* b, int K, int N, int group,
+                   void* stream) {
+  if (!b || !packed || !scales) return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
+  if (K < 1 || N < 2 || N % 2 != 0)
+    return fail(I4G_ERR_SHAPE, "dequantize needs K >= 1 and an even N (K=%d N=%d)", K, N);
+  int st = check_group(K, group, false);
+  if (st != I4G_OK) return st;
+  if (N % 8 == 0 && (!aligned(packed, 4) || !aligned(b, 16)))
+    return fail(I4G_ERR_ALIGNMENT, "packed must be 4-byte and b 16-byte aligned");
+  DeviceInfo* dev = nullptr;
+  if ((st = current_device(&dev)) != I4G_OK) return st;
+  return finish(i4g::prep::dequantize(packed, static_cast<const __half*>(scales),
+                                      static_cast<__half*>(b), K, N, group,
+                                      static_cast<cudaStream_t>(stream)),
+                "dequantize launch");
+}
+
+static int check_128x32(const void* a, const void* b, int K, int N) {
+  if (!a || !b) return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
+  if (K < 32 || N < 128 || K % 32 != 0 || N % 128 != 0)
+    return fail(I4G_ERR_SHAPE, "repack requires K%%32==0 and N%%128==0 (K=%d N=%d)", K, N);
+  return I4G_OK;
+}
+
+int i4g_repack_128x32(const uint8_t* packed, const void* scales, uint8_t* repacked,
+                      void* repacked_scales, int K, int N, int group, void* stream) {
+  int st = check_128x32(packed, repacked, K, N);
+  if (st != I4G_OK) return st;
+  if (!scales || !repacked_scales) return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
+  if ((st = check_group(K, group, true)) != I4G_OK) return st;
+  DeviceInfo* dev = nullptr;
+  if ((st = current_device(&dev)) != I4G_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = i4g::prep::repack_128x32(packed, repacked, K, N, s);
+  if (e == cudaSuccess)
+    e = i4g::prep::repack_scales_128(static_cast<const __half*>(scales),
+                                     static_cast<__half*>(repacked_scales), K, N, group, s);
+  return finish(e, "repack launch");
+}
+
+int i4g_inverse_repack_128x32(const uint8_t* repacked, uint8_t* packed, int K, int N,
+                              void* stream) {
+  int st = check_128x32(repacked, packed, K, N);
+  if (st != I4G_OK) return st;
+  DeviceInfo* dev = nullptr;
+  if ((st = current_device(&dev)) != I4G_OK) return st;
+  return finish(i4g::prep::inverse_repack_128x32(repacked, packed, K, N,
+                                                 static_cast<cudaStream_t>(stream)),
+                "inverse repack launch");
+}
+
+int i4g_repack_mma_128x32(const uint8_t* packed, uint8_t* repacked, int K, int N, void* stream) {
+  int st = check_128x32(packed, repacked, K, N);
+  if (st != I4G_OK) return st;
+  if (!aligned(repacked, 2)) return fail(I4G_ERR_ALIGNMENT, "repacked must be 2-byte aligned");
+  DeviceInfo* dev = nullptr;
+  if ((st = current_device(&dev)) != I4G_OK) return st;
+  return finish(i4g::prep::repack_mma_128x32(packed, repacked, K, N,
+                                             static_cast<cudaStream_t>(stream)),
+                "mma repack launch");
+}
+
+int i4g_repack_mma_pair_128x32(const uint8_t* packed, uint8_t* repacked, int K, int N,
+                               void* stream) {
+  int st = check_128x32(packed, repacked, K, N);
+  if (st != I4G_OK) return st;
+  if (!aligned(repacked, 4)) return fail(I4G_ERR_ALIGNMENT, "repacked must be 4-byte aligned");
+  DeviceInfo* dev = nullptr;
+  if ((st = current_device(&dev)) != I4G_OK) return st;
+  return finish(i4g::prep::repack_mma_pair_128x32(packed, repacked, K, N,
+                                                  static_cast<cudaStream_t>(stream)),
+                "mma pair repack launch");
+}
+
+int i4g_repack_scales_128(const void* scales, void* repacked_scales, int K, int N, int group,
+                          void* stream) {
+  if (!scales || !repacked_scales) return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
+  if (N < 128 || N % 128 != 0 || K < 1)
+    return fail(I4G_ERR_SHAPE, "scale repack requires N%%128==0 (K=%d N=%d)", K, N);
+  int st = check_group(K, group, true);
+  if (st != I4G_OK) return st;
+  DeviceInfo* dev = nullptr;
+  if ((st = current_device(&dev)) != I4G_OK) return st;
+  return finish(i4g::prep::repack_scales_128(static_cast<const __half*>(scales),
+                                             static_cast<__half*>(repacked_scales), K, N, group,
+                                             static_cast<cudaStream_t>(stream)),
+                "scale repack launch");
+}
+
+static int check_umma(const void* a, const void* b, int K, int N) {
+  if (!a || !b) return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
+  if (K < 64 || N < 128 || K % 64 != 0 || N % 128 != 0)
+    return fail(I4G_ERR_SHAPE, "tile layout requires K%%64==0 and N%%128==0 (K=%d N=%d)", K, N);
+  if (!aligned(a, 16) || !aligned(b, 16))
+    return fail(I4G_ERR_ALIGNMENT, "tile layout buffers must be 16-byte aligned");
+  return I4G_OK;
+}
+
+int i4g_repack_umma(const uint8_t* packed, uint8_t* tiles, int K, int N, void* stream) {
+  int st = check_umma(packed, tiles, K, N);
+  if (st != I4G_OK) return st;
+  DeviceInfo* dev = nullptr;
+  if ((st = current_device(&dev)) != I4G_OK) return st;
+  return finish(i4g::prep::repack_umma(packed, tiles, K, N, static_cast<cudaStream_t>(stream)),
+                "tile repack launch");
+}
+
+int i4g_inverse_repack_umma(const uint8_t* tiles, uint8_t* packed, int K, int N, void* stream) {
+  int st = check_umma(tiles, packed, K, N);
+  if (st != I4G_OK) return st;
+  DeviceInfo* dev = nullptr;
+  if ((st = current_device(&dev)) != I4G_OK) return st;
+  return finish(i4g::prep::inverse_repack_umma(tiles, packed, K, N,
+                                               static_cast<cudaStream_t>(stream)),
+                "inverse tile repack launch");
+}
+
+int i4g_gemm(const void* A, const uint8_t* tiles, const void* scales, void* C, int M, int N,
+             int K, int group, void* stream) {
+  return gemm_common(A, tiles, scales, C, false, M, N, K, group, I4G_VARIANT_AUTO, stream);
+}
+
+int i4g_gemm_fp32(const void* A, const uint8_t* tiles, const void* scales, float* C, int M,
+                  int N, int K, int group, void* stream) {
+  return gemm_common(A, tiles, scales, C, true, M, N, K, group, I4G_VARIANT_TC, stream);
+}
+
+int i4g_gemm_variant(const void* A, const uint8_t* tiles, const void* scales, void* C, int M,
+                     int N, int K, int group, int variant, void* stream) {
+  return gemm_common(A, tiles, scales, C, false, M, N, K, group, variant, stream);
+}
+
+int i4g_shard_range(int K, int N, int group, int world, int rank, size_t* tile_offset,
+                    size_t* scale_offset, int* n0, int* n1) {
+  if (!tile_offset || !scale_offset || !n0 || !n1)
+    return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
+  if (world < 1 || rank < 0 || rank >= world)
+    return fail(I4G_ERR_SHAPE, "rank %d out of range for world %d", rank, world);
+  if (K < 64 || K % 64 != 0 || N < 128 || N % (128 * world) != 0)
+    return fail(I4G_ERR_SHAPE, "N=%d must split into %d multiples of 128 (K=%d)", N, world, K);
+  int st = check_group(K, group, true);
+  if (st != I4G_OK) return st;
+  const int n_local = N / world;
+  *n0 = rank * n_local;
+  *n1 = *n0 + n_local;
+  const size_t first_tile = static_cast<size_t>(*n0 / 128);
+  *tile_offset = first_tile * static_cast<size_t>(K / 64) * 4096;
+  *scale_offset = first_tile * static_cast<size_t>(K / group) * 128 * 2;
+  return I4G_OK;
+}
+
+int i4g_device_status(int* out, void* stream) {
+  if (!out) return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
+  DeviceInfo* dev = nullptr;
+  int st = current_device(&dev);
+  if (st != I4G_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int value = 0;
+  cudaError_t e = cudaMemcpyAsync(&value, dev->status_word, sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(dev->status_word, 0, sizeof(int), s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return record_cuda(e, "reading the device status word");
+  *out = value;
+  return I4G_OK;
+}
+
+int i4g_selftest_wait_timeout(unsigned long long limit_ns, void* stream) {
+  DeviceInfo* dev = nullptr;
+  int st = current_device(&dev);
+  if (st != I4G_OK) return st;
+  if (limit_ns == 0 || limit_ns > 1000000000ull)
+    return fail(I4G_ERR_SHAPE, "limit must be in (0, 1 s]");
+  wait_timeout_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(dev->status_word,
+                                                                                limit_ns);
+  return finish(cudaGetLastError(), "self-test launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,45 @@
+// Host-side interface of the kernels (not part of the public C ABI).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace i4g {
+namespace tc {
+// TILE_M (activation rows per tile, the MMA-N) for a problem on sm_count SMs.
+int choose_tile_m(int M, int N, int sm_count);
+cudaError_t launch(const CUtensorMap& act_map, int tile_m, const uint8_t* tiles,
+                   const __half* scales, void* c, bool fp32_out, int M, int N, int K,
+                   int group, int sm_count, int* status, unsigned long long wait_limit_ns,
+                   cudaStream_t stream);
+}  // namespace tc
+
+namespace dec {
+constexpr int MAX_M = 16;
+cudaError_t launch(const __half* a, const uint8_t* tiles, const __half* scales, __half* c,
+                   int M, int N, int K, int group, cudaStream_t stream);
+}  // namespace dec
+
+namespace prep {
+cudaError_t quantize(const __half* b, uint8_t* packed, __half* scales, int K, int N, int group,
+                     cudaStream_t stream);
+cudaError_t dequantize(const uint8_t* packed, const __half* scales, __half* b, int K, int N,
+                       int group, cudaStream_t stream);
+cudaError_t repack_128x32(const uint8_t* packed, uint8_t* repacked, int K, int N,
+                          cudaStream_t stream);
+cudaError_t inverse_repack_128x32(const uint8_t* repacked, uint8_t* packed, int K, int N,
+                                  cudaStream_t stream);
+cudaError_t repack_scales_128(const __half* scales, __half* repacked, int K, int N, int group,
+                              cudaStream_t stream);
+cudaError_t repack_mma_128x32(const uint8_t* packed, uint8_t* repacked, int K, int N,
+                              cudaStream_t stream);
+cudaError_t repack_mma_pair_128x32(const uint8_t* packed, uint8_t* repacked, int K, int N,
+                                   cudaStream_t stream);
+cudaError_t repack_umma(const uint8_t* packed, uint8_t* tiles, int K, int N,
+                        cudaStream_t stream);
+cudaError_t inverse_repack_umma(const uint8_t* tiles, uint8_t* packed, int K, int N,
+                                cudaStream_t stream);
+}  // namespace prep
+}  // namespace i4g

@@ -1,0 +1,340 @@
+// Preprocessing kernels: INT4 quantisation, dequantisation and the weight /
+// scale layouts. All byte and index work; bit-exact against the reference's
+// CPU path (quantize_cpu / dequantize_cpu, src/reference.cu:6-37) and its
+// layouts (include/layout.cuh:8-48).
+//
+// Compiled without fast-math: the quantiser's two divisions (vmax / 7 and
+// x / s) must be IEEE round-to-nearest to reproduce quantize_cpu's codes at
+// rounding ties. (The reference's own GPU quantiser, src/quantize.cu:22,36,
+// is built with --use_fast_math and so may differ from quantize_cpu there.)
+#include "gemm_tc.h"
+
+#include <climits>
+#include <cuda_runtime.h>
+
+namespace i4g {
+namespace prep {
+namespace {
+
+constexpr int THREADS = 256;
+
+__device__ __forceinline__ float max_like_std(float a, float b) { return (a < b) ? b : a; }
+
+// int(x) of an integral float as x86-64 cvttss2si evaluates it in the
+// reference's host build: NaN and out-of-range values give INT_MIN.
+__device__ __forceinline__ int x86_float_to_int(float r) {
+  if (!(r >= -2147483648.0f && r < 2147483648.0f)) return INT_MIN;
+  return static_cast<int>(r);
+}
+
+__device__ __forceinline__ int quantize_one(float x, float s) {
+  int q = x86_float_to_int(rintf(__fdiv_rn(x, s)));
+  q = q < 7 ? q : 7;
+  return q > -8 ? q : -8;
+}
+
+__device__ __forceinline__ int nibble_at(const uint8_t* __restrict__ p, size_t logical) {
+  const uint8_t byte = p[logical >> 1];
+  return (logical & 1) ? (byte >> 4) : (byte & 15);
+}
+
+// One thread per (column pair, group): the group abs-max of two adjacent
+// columns (one 4-byte load per row, coalesced across the warp), the FP16
+// scales, then the codes of those columns, written as whole bytes.
+__global__ void quantize_kernel(const __half2* __restrict__ b, uint8_t* __restrict__ packed,
+                                __half* __restrict__ scales, int K, int N, int group) {
+  const int half_n = N >> 1;
+  const int p = blockIdx.x * blockDim.x + threadIdx.x;
+  const int g = blockIdx.y;
+  if (p >= half_n) return;
+  const int k0 = g * group;
+  const int k1 = min(K, k0 + group);
+  float vmax0 = 0.0f, vmax1 = 0.0f;
+  for (int k = k0; k < k1; ++k) {
+    const float2 x = __half22float2(b[static_cast<size_t>(k) * half_n + p]);
+    vmax0 = max_like_std(vmax0, fabsf(x.x));
+    vmax1 = max_like_std(vmax1, fabsf(x.y));
+  }
+  const __half s0 = __float2half_rn(max_like_std(__fdiv_rn(vmax0, 7.0f), 1.0e-8f));
+  const __half s1 = __float2half_rn(max_like_std(__fdiv_rn(vmax1, 7.0f), 1.0e-8f));
+  scales[static_cast<size_t>(g) * N + 2 * p] = s0;
+  scales[static_cast<size_t>(g) * N + 2 * p + 1] = s1;
+  const float f0 = __half2float(s0), f1 = __half2float(s1);
+  for (int k = k0; k < k1; ++k) {
+    const float2 x = __half22float2(b[static_cast<size_t>(k) * half_n + p]);
+    const int q0 = quantize_one(x.x, f0);
+    const int q1 = quantize_one(x.y, f1);
+    packed[static_cast<size_t>(k) * half_n + p] = static_cast<uint8_t>((q0 & 15) | ((q1 & 15) << 4));
+  }
+}
+
+__device__ __forceinline__ int sext4(int nib) { return ((nib & 15) ^ 8) - 8; }
+
+__device__ __forceinline__ __half dequant_one(int nib, __half s) {
+  return __float2half_rn(static_cast<float>(sext4(nib)) * __half2float(s));
+}
+
+// Eight elements (four bytes) per thread, one 16-byte store. N % 8 == 0.
+__global__ void dequant8_kernel(const uint32_t* __restrict__ packed,
+                                const __half* __restrict__ scales, uint4* __restrict__ b,
+                                size_t chunks, int N, int group) {
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= chunks) return;
+  const size_t e0 = i * 8;
+  const int k = static_cast<int>(e0 / N);
+  const int n = static_cast<int>(e0 - static_cast<size_t>(k) * N);
+  const uint32_t w = packed[i];
+  const __half* srow = scales + static_cast<size_t>(k / group) * N + n;
+  __align__(16) __half out[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) out[j] = dequant_one(static_cast<int>(w >> (4 * j)), srow[j]);
+  b[i] = *reinterpret_cast<const uint4*>(out);
+}
+
+// Generic fallback: two elements (one byte) per thread. N even.
+__global__ void dequant2_kernel(const uint8_t* __restrict__ packed,
+                                const __half* __restrict__ scales, __half* __restrict__ b,
+                                size_t bytes, int N, int group) {
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= bytes) return;
+  const size_t e0 = i * 2;
+  const int k = static_cast<int>(e0 / N);
+  const int n = static_cast<int>(e0 - static_cast<size_t>(k) * N);
+  const uint8_t w = packed[i];
+  const __half* srow = scales + static_cast<size_t>(k / group) * N + n;
+  b[e0] = dequant_one(w & 15, srow[0]);
+  b[e0 + 1] = dequant_one(w >> 4, srow[1]);
+}
+
+// include/layout.cuh:12-20 with BN = 128, BK = 32.
+__device__ __forceinline__ size_t tile128x32_element(int k, int n, int K) {
+  const int nt = n >> 7, kt = k >> 5, ni = n & 127, ki = k & 31;
+  return (static_cast<size_t>(nt) * (K >> 5) + kt) * 4096 + ki * 128 + ni;
+}
+
+// One output byte (two adjacent columns of one k row) per thread.
+__global__ void repack_128x32_kernel(const uint8_t* __restrict__ packed,
+                                     uint8_t* __restrict__ out, size_t bytes, int K, int N) {
+  const size_t o = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (o >= bytes) return;
+  const size_t e0 = o * 2;
+  const size_t tile = e0 >> 12;
+  const int within = static_cast<int>(e0 & 4095);
+  const int ktiles = K >> 5;
+  const int nt = static_cast<int>(tile / ktiles);
+  const int kt = static_cast<int>(tile - static_cast<size_t>(nt) * ktiles);
+  const int k = kt * 32 + (within >> 7);
+  const int n = nt * 128 + (within & 127);
+  const size_t logical = static_cast<size_t>(k) * N + n;
+  out[o] = static_cast<uint8_t>(nibble_at(packed, logical) | (nibble_at(packed, logical + 1) << 4));
+}
+
+__global__ void inverse_repack_128x32_kernel(const uint8_t* __restrict__ rep,
+                                             uint8_t* __restrict__ out, size_t bytes, int K,
+                                             int N) {
+  const size_t o = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (o >= bytes) return;
+  const size_t e0 = o * 2;
+  const int k = static_cast<int>(e0 / N);
+  const int n = static_cast<int>(e0 - static_cast<size_t>(k) * N);
+  out[o] = static_cast<uint8_t>(nibble_at(rep, tile128x32_element(k, n, K)) |
+                                (nibble_at(rep, tile128x32_element(k, n + 1, K)) << 4));
+}
+
+// [K/g][N] -> [N/128][K/g][128] (include/layout.cuh:27-32).
+__global__ void repack_scales_128_kernel(const __half* __restrict__ src, __half* __restrict__ dst,
+                                         size_t count, int N, int groups) {
+  const size_t o = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (o >= count) return;
+  const int ni = static_cast<int>(o & 127);
+  const size_t x = o >> 7;
+  const int g = static_cast<int>(x % groups);
+  const int nt = static_cast<int>(x / groups);
+  dst[o] = src[static_cast<size_t>(g) * N + nt * 128 + ni];
+}
+
+// Four nibbles {k0, k0+1, k0+8, k0+9} of column n: one lane's mma.m16n8k16
+// B-fragment word (include/layout.cuh:34-40).
+__device__ __forceinline__ uint32_t mma_word(const uint8_t* __restrict__ p, int k0, int n,
+                                             int N) {
+  const size_t base = static_cast<size_t>(k0) * N + n;
+  return static_cast<uint32_t>(nibble_at(p, base) | (nibble_at(p, base + N) << 4) |
+                               (nibble_at(p, base + 8 * static_cast<size_t>(N)) << 8) |
+                               (nibble_at(p, base + 9 * static_cast<size_t>(N)) << 12));
+}
+
+// Word order [k16][warp_n][n8][lane] inside each 32x128 tile.
+__global__ void repack_mma_kernel(const uint8_t* __restrict__ packed, uint16_t* __restrict__ out,
+                                  size_t words, int K, int N) {
+  const size_t o = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (o >= words) return;
+  const size_t tile = o >> 10;
+  const int within = static_cast<int>(o & 1023);
+  const int lane = within & 31, n8 = (within >> 5) & 7, wn = (within >> 8) & 1, k16 = within >> 9;
+  const int ktiles = K >> 5;
+  const int nt = static_cast<int>(tile / ktiles);
+  const int kt = static_cast<int>(tile - static_cast<size_t>(nt) * ktiles);
+  const int n = nt * 128 + wn * 64 + n8 * 8 + (lane >> 2);
+  const int k0 = kt * 32 + k16 * 16 + (lane & 3) * 2;
+  out[o] = static_cast<uint16_t>(mma_word(packed, k0, n, N));
+}
+
+// Word order [warp_n][n8][lane], k16 = 0 in the low half, 1 in the high half.
+__global__ void repack_mma_pair_kernel(const uint8_t* __restrict__ packed,
+                                       uint32_t* __restrict__ out, size_t pairs, int K, int N) {
+  const size_t o = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (o >= pairs) return;
+  const size_t tile = o >> 9;
+  const int within = static_cast<int>(o & 511);
+  const int lane = within & 31, n8 = (within >> 5) & 7, wn = within >> 8;
+  const int ktiles = K >> 5;
+  const int nt = static_cast<int>(tile / ktiles);
+  const int kt = static_cast<int>(tile - static_cast<size_t>(nt) * ktiles);
+  const int n = nt * 128 + wn * 64 + n8 * 8 + (lane >> 2);
+  const int k0 = kt * 32 + (lane & 3) * 2;
+  out[o] = mma_word(packed, k0, n, N) | (mma_word(packed, k0 + 16, n, N) << 16);
+}
+
+// Tile layout for the sm_100a kernels, one 128-column x 64-k block per CTA.
+// The block's 64 rows x 64 bytes of row-major nibbles are staged in shared
+// memory with 16-byte coalesced loads; each output word then gathers the
+// eight k of one column: element k%8 = 2p + hi at bit 4p + 16hi.
+__global__ void repack_umma_kernel(const uint8_t* __restrict__ packed, uint32_t* __restrict__ out,
+                                   int K, int N) {
+  __shared__ uint4 stage[64 * 4];  // [k][64 bytes]
+  const int kblocks = K >> 6;
+  const int blk = blockIdx.x;
+  const int nt = blk / kblocks, kb = blk - nt * kblocks;
+  const size_t row_bytes = static_cast<size_t>(N) >> 1;
+  for (int i = threadIdx.x; i < 64 * 4; i += blockDim.x) {
+    const int k = i >> 2, c = i & 3;
+    stage[i] = *reinterpret_cast<const uint4*>(packed + static_cast<size_t>(kb * 64 + k) * row_bytes +
+                                               nt * 64 + c * 16);
+  }
+  __syncthreads();
+  const uint8_t* sb = reinterpret_cast<const uint8_t*>(stage);
+  uint32_t* dst = out + static_cast<size_t>(blk) * 1024;
+  for (int wi = threadIdx.x; wi < 1024; wi += blockDim.x) {
+    const int h = wi >> 9, ni = (wi >> 2) & 127, w = wi & 3;
+    const int kk0 = h * 32 + w * 8;
+    uint32_t word = 0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const uint8_t byte = sb[(kk0 + e) * 64 + (ni >> 1)];
+      const uint32_t nib = (ni & 1) ? (byte >> 4) : (byte & 15);
+      word |= nib << (4 * (e >> 1) + 16 * (e & 1));
+    }
+    dst[wi] = word;
+  }
+}
+
+__global__ void inverse_repack_umma_kernel(const uint32_t* __restrict__ tiles,
+                                           uint8_t* __restrict__ packed, int K, int N) {
+  __shared__ uint32_t stage[1024];
+  const int kblocks = K >> 6;
+  const int blk = blockIdx.x;
+  const int nt = blk / kblocks, kb = blk - nt * kblocks;
+  for (int i = threadIdx.x; i < 1024; i += blockDim.x)
+    stage[i] = tiles[static_cast<size_t>(blk) * 1024 + i];
+  __syncthreads();
+  const size_t row_bytes = static_cast<size_t>(N) >> 1;
+  for (int i = threadIdx.x; i < 64 * 64; i += blockDim.x) {
+    const int kk = i >> 6, byte = i & 63;
+    const int h = kk >> 5, w = (kk & 31) >> 3, e = kk & 7;
+    const int shift = 4 * (e >> 1) + 16 * (e & 1);
+    uint32_t v = 0;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int ni = byte * 2 + j;
+      v |= ((stage[h * 512 + ni * 4 + w] >> shift) & 15u) << (4 * j);
+    }
+    packed[static_cast<size_t>(kb * 64 + kk) * row_bytes + nt * 64 + byte] = static_cast<uint8_t>(v);
+  }
+}
+
+inline unsigned blocks_for(size_t n) { return static_cast<unsigned>((n + THREADS - 1) / THREADS); }
+
+}  // namespace
+
+cudaError_t quantize(const __half* b, uint8_t* packed, __half* scales, int K, int N, int group,
+                     cudaStream_t stream) {
+  const int groups = (K + group - 1) / group;
+  const int pairs = N / 2;
+  const dim3 grid((pairs + 127) / 128, groups);
+  quantize_kernel<<<grid, 128, 0, stream>>>(reinterpret_cast<const __half2*>(b), packed, scales, K,
+                                            N, group);
+  return cudaGetLastError();
+}
+
+cudaError_t dequantize(const uint8_t* packed, const __half* scales, __half* b, int K, int N,
+                       int group, cudaStream_t stream) {
+  const size_t elements = static_cast<size_t>(K) * N;
+  if (N % 8 == 0) {
+    const size_t chunks = elements / 8;
+    dequant8_kernel<<<blocks_for(chunks), THREADS, 0, stream>>>(
+        reinterpret_cast<const uint32_t*>(packed), scales, reinterpret_cast<uint4*>(b), chunks, N,
+        group);
+  } else {
+    const size_t bytes = elements / 2;
+    dequant2_kernel<<<blocks_for(bytes), THREADS, 0, stream>>>(packed, scales, b, bytes, N, group);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t repack_128x32(const uint8_t* packed, uint8_t* repacked, int K, int N,
+                          cudaStream_t stream) {
+  const size_t bytes = static_cast<size_t>(K) * N / 2;
+  repack_128x32_kernel<<<blocks_for(bytes), THREADS, 0, stream>>>(packed, repacked, bytes, K, N);
+  return cudaGetLastError();
+}
+
+cudaError_t inverse_repack_128x32(const uint8_t* repacked, uint8_t* packed, int K, int N,
+                                  cudaStream_t stream) {
+  const size_t bytes = static_cast<size_t>(K) * N / 2;
+  inverse_repack_128x32_kernel<<<blocks_for(bytes), THREADS, 0, stream>>>(repacked, packed, bytes,
+                                                                          K, N);
+  return cudaGetLastError();
+}
+
+cudaError_t repack_scales_128(const __half* scales, __half* repacked, int K, int N, int group,
+                              cudaStream_t stream) {
+  const int groups = K / group;
+  const size_t count = static_cast<size_t>(groups) * N;
+  repack_scales_128_kernel<<<blocks_for(count), THREADS, 0, stream>>>(scales, repacked, count, N,
+                                                                      groups);
+  return cudaGetLastError();
+}
+
+cudaError_t repack_mma_128x32(const uint8_t* packed, uint8_t* repacked, int K, int N,
+                              cudaStream_t stream) {
+  const size_t words = static_cast<size_t>(K) * N / 4;
+  repack_mma_kernel<<<blocks_for(words), THREADS, 0, stream>>>(
+      packed, reinterpret_cast<uint16_t*>(repacked), words, K, N);
+  return cudaGetLastError();
+}
+
+cudaError_t repack_mma_pair_128x32(const uint8_t* packed, uint8_t* repacked, int K, int N,
+                                   cudaStream_t stream) {
+  const size_t pairs = static_cast<size_t>(K) * N / 8;
+  repack_mma_pair_kernel<<<blocks_for(pairs), THREADS, 0, stream>>>(
+      packed, reinterpret_cast<uint32_t*>(repacked), pairs, K, N);
+  return cudaGetLastError();
+}
+
+cudaError_t repack_umma(const uint8_t* packed, uint8_t* tiles, int K, int N, cudaStream_t stream) {
+  const int blocks = (N / 128) * (K / 64);
+  repack_umma_kernel<<<blocks, THREADS, 0, stream>>>(packed, reinterpret_cast<uint32_t*>(tiles), K,
+                                                     N);
+  return cudaGetLastError();
+}
+
+cudaError_t inverse_repack_umma(const uint8_t* tiles, uint8_t* packed, int K, int N,
+                                cudaStream_t stream) {
+  const int blocks = (N / 128) * (K / 64);
+  inverse_repack_umma_kernel<<<blocks, THREADS, 0, stream>>>(
+      reinterpret_cast<const uint32_t*>(tiles), packed, K, N);
+  return cudaGetLastError();
+}
+
+}  // namespace prep
+}  // namespace i4g

@@ -1,0 +1,65 @@
+"""Column-parallel (N-sharded) W4A16 GEMM over torch.distributed.
+
+Each rank owns an N/world slice of the packed weights and scales (a
+contiguous byte range of the tile and scale layouts, see ``shard_range``);
+the activations A are replicated. The GEMM itself needs no communication.
+Only when one rank needs the full C does a collective run: an all-gather of
+the FP16 C column blocks (NCCL over NVLink on GPUs, gloo on CPU in tests),
+which yields the rank-major ``[world][M][N/world]`` buffer that
+``assemble_columns`` turns into row-major ``[M][N]``.
+
+The reference has no multi-GPU path; this is the north star's harness for
+configs 3 and 4 (M=8192, K=8192, N=28672; K=8192, N=57344, g64, 8 GPUs).
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from .linear import QuantizedLinear
+
+
+def assemble_columns(gathered: torch.Tensor, world: int, M: int, n_local: int,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    """[world * M * n_local] rank-major blocks -> row-major [M, world * n_local]."""
+    blocks = gathered.view(world, M, n_local)
+    if out is None:
+        out = torch.empty(M, world * n_local, dtype=gathered.dtype, device=gathered.device)
+    out.view(M, world, n_local).copy_(blocks.permute(1, 0, 2))
+    return out
+
+
+def gather_columns(c_local: torch.Tensor, group=None, out: torch.Tensor | None = None,
+                   gathered: torch.Tensor | None = None) -> torch.Tensor:
+    """All-gather every rank's [M, n_local] block into the full [M, N] C."""
+    world = dist.get_world_size(group)
+    M, n_local = c_local.shape
+    if gathered is None:
+        gathered = torch.empty(world * M * n_local, dtype=c_local.dtype, device=c_local.device)
+    dist.all_gather_into_tensor(gathered, c_local.contiguous().view(-1), group=group)
+    return assemble_columns(gathered, world, M, n_local, out)
+
+
+class ColumnParallelLinear:
+    """This rank's column slice of a quantised weight, plus the optional gather."""
+
+    def __init__(self, local: QuantizedLinear, world: int, rank: int, group=None):
+        self.local = local
+        self.world, self.rank, self.group = world, rank, group
+        self.n0 = rank * local.N
+        self.N = world * local.N
+
+    @classmethod
+    def from_full(cls, full: QuantizedLinear, group=None) -> "ColumnParallelLinear":
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        rank = dist.get_rank(group) if dist.is_initialized() else 0
+        return cls(full.shard(world, rank), world, rank, group)
+
+    def forward_local(self, a: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        return self.local(a, out=out)
+
+    def forward(self, a: torch.Tensor, gather: bool = True) -> torch.Tensor:
+        c_local = self.forward_local(a)
+        if not gather or self.world == 1:
+            return c_local
+        return gather_columns(c_local, self.group)

@@ -1,0 +1,231 @@
+"""Parity of the CUDA path (through the C ABI) with the reference's CPU path.
+
+Byte and index work (quantize codes and scales, dequantize, every weight
+layout) is compared bit-exactly with the golden fixtures made by the
+reference itself and with the oracle. The GEMM is compared with the oracle
+under the tolerance stated in tests/parity.py (<= 1 FP16 ulp, widened only by
+the FP32 summation-order bound where that exceeds an ulp).
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import golden_names, load_golden
+from parity import fp32_report, gemm_report, make_inputs, u16
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def i4g():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    import sm_120__gemm_b200 as m
+    m.load()
+    return m
+
+
+def dev_u16(arr):
+    return torch.from_numpy(np.ascontiguousarray(arr).view(np.int16)).cuda().view(torch.float16)
+
+
+def dev_u8(arr):
+    return torch.from_numpy(np.ascontiguousarray(arr, dtype=np.uint8)).cuda()
+
+
+def gpu_quantize(i4g, b16_u16, K, N, group):
+    b = dev_u16(b16_u16.reshape(K, N))
+    packed = torch.empty(K * N // 2, dtype=torch.uint8, device="cuda")
+    scales = torch.empty((K + group - 1) // group, N, dtype=torch.float16, device="cuda")
+    i4g.launch_quantize(b, packed, scales, K, N, group)
+    torch.cuda.synchronize()
+    return packed, scales
+
+
+# ------------------------------------------------------------ byte exactness
+
+@pytest.mark.parametrize("name", golden_names("quant_"))
+def test_quantize_bit_exact(i4g, name):
+    g = load_golden(name)
+    packed, scales = gpu_quantize(i4g, g["b"], g["K"], g["N"], g["group"])
+    np.testing.assert_array_equal(u16(scales), g["scales"])
+    np.testing.assert_array_equal(packed.cpu().numpy(), g["packed"])
+
+
+@pytest.mark.parametrize("name", golden_names("quant_"))
+def test_dequantize_bit_exact(i4g, name):
+    g = load_golden(name)
+    K, N = g["K"], g["N"]
+    out = torch.empty(K, N, dtype=torch.float16, device="cuda")
+    i4g.launch_dequantize(dev_u8(g["packed"]), dev_u16(g["scales"]), out, K, N, g["group"])
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(u16(out), g["dequant"])
+
+
+@pytest.mark.parametrize("name", golden_names("layout_"))
+def test_reference_layouts_bit_exact(i4g, name):
+    g = load_golden(name)
+    K, N, grp = g["K"], g["N"], g["group"]
+    packed = dev_u8(g["packed"])
+    nbytes = K * N // 2
+    tile = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    rsc = torch.empty((K // grp) * N, dtype=torch.float16, device="cuda")
+    i4g.launch_repack_128x32(packed, dev_u16(g["scales"]), tile, rsc, K, N, grp)
+    mma = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    i4g.launch_repack_mma_128x32(packed, mma, K, N)
+    pair = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    i4g.launch_repack_mma_pair_128x32(packed, pair, K, N)
+    rsc2 = torch.empty_like(rsc)
+    i4g.launch_repack_scales_128(dev_u16(g["scales"]), rsc2, K, N, grp)
+    inv = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    i4g.launch_inverse_repack_128x32(tile, inv, K, N)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(tile.cpu().numpy(), g["tile"])
+    np.testing.assert_array_equal(mma.cpu().numpy(), g["mma"])
+    np.testing.assert_array_equal(pair.cpu().numpy(), g["pair"])
+    np.testing.assert_array_equal(u16(rsc), g["scales128"])
+    np.testing.assert_array_equal(u16(rsc2), g["scales128"])
+    np.testing.assert_array_equal(inv.cpu().numpy(), g["packed"])
+
+
+@pytest.mark.parametrize("K,N", [(64, 128), (192, 384), (4096, 512)])
+def test_tile_layout_matches_oracle(i4g, K, N):
+    rng = np.random.default_rng(K + N)
+    packed_np = rng.integers(0, 256, K * N // 2, dtype=np.uint8)
+    tiles = torch.empty(K * N // 2, dtype=torch.uint8, device="cuda")
+    i4g.launch_repack_umma(dev_u8(packed_np), tiles, K, N)
+    back = torch.empty_like(tiles)
+    i4g.launch_inverse_repack_umma(tiles, back, K, N)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(tiles.cpu().numpy(), oracle.repack_umma(packed_np, K, N))
+    np.testing.assert_array_equal(back.cpu().numpy(), packed_np)
+
+
+def test_quantize_large_matches_oracle(i4g):
+    K, N = 4096, 4096
+    _, w = make_inputs(1, N, K)
+    w16 = u16(w)
+    for grp in (32, 64, 128):
+        packed, scales = gpu_quantize(i4g, w16, K, N, grp)
+        p_ref, s_ref = oracle.quantize(w16, K, N, grp)
+        np.testing.assert_array_equal(u16(scales), s_ref)
+        np.testing.assert_array_equal(packed.cpu().numpy(), p_ref)
+
+
+# ------------------------------------------------------------------- GEMM
+
+def prepared(i4g, g):
+    """GPU quantize + repack of a golden case; returns device buffers."""
+    K, N, grp = g["K"], g["N"], g["group"]
+    packed, scales = gpu_quantize(i4g, g["b"], K, N, grp)
+    np.testing.assert_array_equal(packed.cpu().numpy(), g["packed"])
+    lin = i4g.QuantizedLinear.from_packed(packed, scales, K, N, grp)
+    return lin
+
+
+def oracle_abs(g):
+    deq = oracle.dequantize(g["packed"], g["scales"], g["K"], g["N"], g["group"])
+    return oracle.abs_gemm_rows(g["a"], deq, g["M"], g["N"], g["K"])
+
+
+@pytest.mark.parametrize("name", golden_names("gemm_"))
+def test_gemm_golden(i4g, name):
+    g = load_golden(name)
+    M, N, K = g["M"], g["N"], g["K"]
+    lin = prepared(i4g, g)
+    a = dev_u16(g["a"])
+    abs32 = oracle_abs(g)
+    variants = [i4g.VARIANT_TC] + ([i4g.VARIANT_DECODE] if M <= 16 else [])
+    for variant in variants:
+        c = torch.empty(M, N, dtype=torch.float16, device="cuda")
+        i4g.launch_gemm_variant(a, lin.tiles, lin.scales, c, M, N, K, g["group"], variant)
+        torch.cuda.synchronize()
+        assert i4g.device_status() == 0
+        rep = gemm_report(u16(c), g["c32"], abs32, K)
+        print(name, "variant", variant, rep)
+        assert rep["ok"], rep
+
+
+@pytest.mark.parametrize("name", ["gemm_m64_n128_k128_g32", "gemm_m200_n384_k192_g64",
+                                  "gemm_m5_n256_k256_g64"])
+def test_gemm_fp32_output(i4g, name):
+    g = load_golden(name)
+    M, N, K = g["M"], g["N"], g["K"]
+    lin = prepared(i4g, g)
+    c = lin(dev_u16(g["a"]), fp32_out=True)
+    torch.cuda.synchronize()
+    rep = fp32_report(c.cpu().numpy(), g["c32"], oracle_abs(g), K)
+    print(name, rep)
+    assert rep["ok"], rep
+
+
+def run_case(i4g, M, N, K, grp, rows=None, a_dist="uniform", variant=0, seed=0):
+    a, w = make_inputs(M, N, K, seed_a=1234 + seed, seed_b=5678 + seed, a_dist=a_dist)
+    w16 = u16(w)
+    a16 = u16(a)
+    packed_np, scales_np = oracle.quantize(w16, K, N, grp)
+    lin = i4g.QuantizedLinear.from_weight(w.cuda(), grp)
+    c = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    i4g.launch_gemm_variant(a.cuda(), lin.tiles, lin.scales, c, M, N, K, grp, variant)
+    torch.cuda.synchronize()
+    assert i4g.device_status() == 0
+    got = u16(c)
+    deq = oracle.dequantize(packed_np, scales_np, K, N, grp)
+    rows = np.arange(M) if rows is None else np.asarray(rows)
+    ref32 = oracle.gemm_rows(a16, deq, M, N, K, rows=rows, threads=8)
+    abs32 = oracle.abs_gemm_rows(a16, deq, M, N, K, rows=rows)
+    rep = gemm_report(got[rows], ref32, abs32, K)
+    return rep, c
+
+
+@pytest.mark.parametrize("grp", [32, 64, 128])
+def test_gemm_4096_sampled_rows(i4g, grp):
+    M = N = K = 4096
+    rows = np.concatenate([np.arange(0, 8), np.arange(185, 200), np.arange(4088, 4096),
+                           np.random.default_rng(grp).choice(4096, 16, replace=False)])
+    rep, _ = run_case(i4g, M, N, K, grp, rows=rows)
+    print("4096^3 g", grp, rep)
+    assert rep["ok"], rep
+
+
+@pytest.mark.parametrize("M", [1, 4, 8, 16])
+@pytest.mark.parametrize("K,N", [(4096, 14336), (14336, 4096)])
+def test_gemm_decode_shapes(i4g, M, K, N):
+    rep, _ = run_case(i4g, M, N, K, 128, a_dist="normal")
+    print("decode", M, K, N, rep)
+    assert rep["ok"], rep
+
+
+@pytest.mark.parametrize("M,N,K,grp", [(17, 256, 256, 32), (100, 384, 512, 64),
+                                       (333, 640, 320, 64), (1000, 256, 1024, 128),
+                                       (64, 128, 64, 32), (3, 128, 64, 64)])
+def test_gemm_ragged_shapes(i4g, M, N, K, grp):
+    rep, _ = run_case(i4g, M, N, K, grp)
+    print("ragged", M, N, K, grp, rep)
+    assert rep["ok"], rep
+
+
+def test_gemm_deterministic(i4g):
+    M = N = K = 1024
+    _, c0 = run_case(i4g, M, N, K, 64, rows=np.arange(4))
+    outs = []
+    a, w = make_inputs(M, N, K)
+    lin = i4g.QuantizedLinear.from_weight(w.cuda(), 64)
+    ad = a.cuda()
+    for _ in range(5):
+        outs.append(lin(ad).clone())
+    torch.cuda.synchronize()
+    for o in outs[1:]:
+        assert torch.equal(o.view(torch.int16), outs[0].view(torch.int16))
+    assert torch.equal(outs[0].view(torch.int16), c0.view(torch.int16))
+
+
+def test_wait_timeout_is_reported_not_faulted(i4g):
+    assert i4g.device_status() == 0
+    i4g.selftest_wait_timeout(2_000_000)  # 2 ms limit on a barrier nobody completes
+    assert i4g.device_status() == -8
+    assert i4g.device_status() == 0  # reading clears it
+    # the context is still usable
+    rep, _ = run_case(i4g, 64, 128, 128, 32)
+    assert rep["ok"], rep

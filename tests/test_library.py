@@ -1,0 +1,109 @@
+"""The C-ABI library without a GPU: it loads, exports every entry point that
+include/i4g.h declares, and rejects bad arguments before touching a device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "i4g.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\*?\s+\*?(i4g_\w+)\s*\(", text, re.M)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    import sm_120__gemm_b200 as m
+    return m.load()
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    for expected in ("i4g_quantize", "i4g_dequantize", "i4g_repack_umma", "i4g_gemm",
+                     "i4g_gemm_fp32", "i4g_repack_mma_pair_128x32", "i4g_shard_range"):
+        assert expected in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_status_strings(lib):
+    for code in range(0, -10, -1):
+        assert lib.i4g_status_string(code)
+    assert lib.i4g_layout_version() == 1
+
+
+def test_argument_checks_need_no_gpu(lib):
+    vp = ctypes.c_void_p
+    fake = vp(0x1000)  # never dereferenced: checks fail first
+    # null pointers
+    assert lib.i4g_gemm(None, fake, fake, fake, 64, 128, 128, 64, None) == -1
+    # unsupported group (the reference silently used g128 for these)
+    for g in (0, 16, 96, 256):
+        assert lib.i4g_gemm(fake, fake, fake, fake, 64, 128, 128, g, None) == -3
+    # K not a multiple of the group
+    assert lib.i4g_gemm(fake, fake, fake, fake, 64, 128, 192, 128, None) == -3
+    # shapes
+    assert lib.i4g_gemm(fake, fake, fake, fake, 0, 128, 128, 64, None) == -2
+    assert lib.i4g_gemm(fake, fake, fake, fake, 64, 100, 128, 64, None) == -2
+    assert lib.i4g_gemm(fake, fake, fake, fake, 64, 128, 96, 32, None) == -2
+    # alignment
+    assert lib.i4g_gemm(vp(0x1002), fake, fake, fake, 64, 128, 128, 64, None) == -4
+    # unknown variant / decode beyond M=16
+    assert lib.i4g_gemm_variant(fake, fake, fake, fake, 64, 128, 128, 64, 7, None) == -9
+    assert lib.i4g_gemm_variant(fake, fake, fake, fake, 17, 128, 128, 64, 2, None) == -9
+    # preprocessing shapes
+    assert lib.i4g_quantize(fake, fake, fake, 128, 127, 32, None) == -2
+    assert lib.i4g_repack_umma(fake, fake, 96, 128, None) == -2
+    assert lib.i4g_repack_128x32(fake, fake, fake, fake, 128, 100, 32, None) == -2
+
+
+def test_shard_range_arithmetic():
+    import sm_120__gemm_b200 as m
+    K, N, g = 8192, 28672, 128
+    for world in (1, 2, 4, 8):
+        prev_end = 0
+        for rank in range(world):
+            toff, soff, n0, n1 = m.shard_range(K, N, g, world, rank)
+            assert n0 == prev_end and n1 - n0 == N // world
+            assert toff == n0 * K // 2
+            assert soff == (n0 // 128) * (K // g) * 128 * 2
+            prev_end = n1
+        assert prev_end == N
+    with pytest.raises(m.I4GError):
+        m.shard_range(K, 28672 + 128, g, 8, 0)
+
+
+def test_cpp_wrappers_compile_and_throw(tmp_path):
+    """include/int4gemm.hpp keeps the reference's C++ signatures and turns a
+    non-zero status into std::runtime_error (checked without a GPU)."""
+    import shutil
+    import subprocess
+    if shutil.which("g++") is None:
+        pytest.skip("no host C++ compiler")
+    src = tmp_path / "t.cpp"
+    src.write_text(r'''
+#include "int4gemm.hpp"
+#include <cstdio>
+int main() {
+  int4gemm::KernelLaunch fn = &int4gemm::launch_final;  // reference signature
+  try { fn(nullptr, nullptr, nullptr, nullptr, 64, 128, 128, 64, nullptr); }
+  catch (const std::runtime_error& e) { std::printf("threw: %s\n", e.what()); return 0; }
+  return 1;
+}
+''')
+    exe = tmp_path / "t"
+    pkg = os.path.join(ROOT, "sm_120__gemm_b200")
+    subprocess.run(["g++", "-std=c++17", "-I", os.path.join(ROOT, "include"),
+                    "-I", "/usr/local/cuda/include", str(src), "-o", str(exe),
+                    "-L", pkg, "-li4g", f"-Wl,-rpath,{pkg}"], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert out.returncode == 0, out
+    assert "null pointer" in out.stdout
