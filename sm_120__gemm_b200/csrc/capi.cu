@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -167,6 +168,17 @@ int act_map(const void* A, int M, int K, int tile_m, const CUtensorMap** out) {
 
 unsigned long long g_wait_limit_ns = kDefaultWaitLimitNs;
 
+// Tuning override for the tcgen05 kernel's activation tile (64, 128 or 192
+// rows), read once from I4G_TILE_M; 0 means the shape-based choice.
+int tile_m_override() {
+  static const int v = [] {
+    const char* e = std::getenv("I4G_TILE_M");
+    const int t = e ? std::atoi(e) : 0;
+    return (t == 64 || t == 128 || t == 192) ? t : 0;
+  }();
+  return v;
+}
+
 int gemm_common(const void* A, const uint8_t* tiles, const void* scales, void* C, bool fp32_out,
                 int M, int N, int K, int group, int variant, void* stream) {
   if (!A || !tiles || !scales || !C) return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
@@ -194,9 +206,10 @@ int gemm_common(const void* A, const uint8_t* tiles, const void* scales, void* C
   const __half* sc = static_cast<const __half*>(scales);
   if (variant == I4G_VARIANT_DECODE)
     return finish(i4g::dec::launch(static_cast<const __half*>(A), tiles, sc,
-                                   static_cast<__half*>(C), M, N, K, group, s),
+                                   static_cast<__half*>(C), M, N, K, group, dev->sm_count, s),
                   "decode kernel launch");
-  const int tile_m = i4g::tc::choose_tile_m(M, N, dev->sm_count);
+  const int tile_m = tile_m_override() ? tile_m_override()
+                                       : i4g::tc::choose_tile_m(M, N, dev->sm_count);
   const CUtensorMap* map = nullptr;
   st = act_map(A, M, K, tile_m, &map);
   if (st != I4G_OK) return st;

@@ -9,23 +9,29 @@
 // Formulation (swap-AB). The MMA computes D[n][m] = sum_k W[n][k] * A[m][k]:
 //   MMA-M = 128 weight columns n      operand A from TMEM (dequantised here)
 //   MMA-N = TILE_M activation rows m  operand B from SMEM (TMA, 128B swizzle)
-//   D     = TILE_M fp32 TMEM columns, double-buffered so the epilogue of one
-//           tile overlaps the main loop of the next.
+//   D     = TILE_M fp32 TMEM columns
 // Putting the weights on the MMA-M side means every dequantised weight is
 // used by TILE_M activation rows, and the dequantised FP16 values never touch
 // shared memory: each dequant thread owns one TMEM lane (one weight column)
-// and writes it with tcgen05.st.
+// and writes it with tcgen05.st. A tcgen05.mma of M=128, K=16 costs about the
+// same issue time at any N up to 256, so the main shape uses N = 256.
 //
-// Warp roles (448 threads, one CTA per SM, persistent over output tiles):
-//   warp 0      TMA producer: activation box + packed weight block + scales
-//   warp 1      TMEM allocator and the single MMA-issuing thread
-//   warps 2-9   dequant: smem nibbles -> half(q*s) -> TMEM weight stage
-//   warps 10-13 epilogue: TMEM -> registers -> FP16 -> global C
+// Warp roles (one CTA per SM, persistent over output tiles):
+//   warp 0       activation producer: TMA of a 64-k x TILE_M box
+//   warp 1       TMEM allocator and the single MMA-issuing thread
+//   warp 2       weight producer: bulk copies of packed nibbles and scales
+//   warps 3-10   dequant, two groups of four warps; group g takes the 64-k
+//                blocks with index % 2 == g, each thread turning one weight
+//                column's 64 nibbles into 64 halves (one tcgen05.st)
+//   warps 11-26  epilogue: TMEM -> registers -> FP16 (or FP32) -> global C
 //
-// Pipelines (all mbarrier based, every wait bounded):
-//   full[s]/empty[s]    smem stages (activation, packed weights, scales)
-//   wfull[w]/wempty[w]  TMEM weight stages (32 columns = 64 k each)
-//   afull[a]/aempty[a]  TMEM accumulators
+// Pipelines (mbarriers, every wait bounded):
+//   afull/aempty[A_STAGES]  activation boxes in smem (freed by MMA completion)
+//   wfull/wempty[W_STAGES]  packed weight blocks in smem (freed once read)
+//   tfull/tempty[T_STAGES]  dequantised weight stages in TMEM
+//   dfull/dempty[ACC]       accumulators in TMEM
+// The weight ring does not wait for the tensor core, so the dequant runs
+// ahead of the MMA by up to T_STAGES blocks.
 #include "ptx.cuh"
 #include "gemm_tc.h"
 
@@ -36,33 +42,38 @@ namespace tc {
 
 constexpr int TILE_N = 128;         // weight columns per tile (MMA-M)
 constexpr int BK = 64;              // k per stage (one 128-byte swizzle row)
-constexpr int W_STAGES = 4;         // TMEM weight stages
-constexpr int W_COLS = 32;          // TMEM columns per weight stage (64 halves)
-constexpr int NUM_DEQ_WARPS = 8;
-constexpr int NUM_EPI_WARPS = 4;
-constexpr int THREADS = 32 * (2 + NUM_DEQ_WARPS + NUM_EPI_WARPS);
+constexpr int T_COLS = 32;          // TMEM columns per dequantised weight stage (64 halves)
+constexpr int T_STAGES = 8;         // TMEM weight stages
+constexpr int DEQ_GROUPS = 2;       // dequant warp groups (4 warps = 128 lanes each)
+constexpr int NUM_DEQ_WARPS = 4 * DEQ_GROUPS;
+constexpr int NUM_EPI_WARPS = 16;   // four per TMEM lane quarter
+constexpr int FIRST_DEQ_WARP = 3;
+constexpr int FIRST_EPI_WARP = FIRST_DEQ_WARP + NUM_DEQ_WARPS;
+constexpr int THREADS = 32 * (FIRST_EPI_WARP + NUM_EPI_WARPS);
 constexpr int TMEM_COLS = 512;
-constexpr int ACC_COL0 = W_STAGES * W_COLS;  // 128
+constexpr int ACC_COL0 = T_STAGES * T_COLS;    // 256
 constexpr int WBLOCK_BYTES = TILE_N * BK / 2;  // 4096: one tile-layout block
-constexpr int SCALE_BYTES = 512;            // up to two groups x 128 halves
-constexpr int GROUP_M = 16;                 // rasterisation band (m-tiles)
+constexpr int SCALE_BYTES = 512;               // up to two groups x 128 halves
+constexpr int W_SLOT = WBLOCK_BYTES + SCALE_BYTES;
+constexpr int W_STAGES = 8;
+constexpr int GROUP_M = 8;                     // rasterisation band (m-tiles)
 
 template <int TILE_M>
-struct Smem {
+struct Cfg {
+  static constexpr int ACC = TILE_M <= 128 ? 2 : 1;  // accumulators in TMEM
   static constexpr int ACT_BYTES = TILE_M * BK * 2;
-  static constexpr int STAGES = TILE_M >= 192 ? 6 : (TILE_M >= 128 ? 8 : 10);
+  static constexpr int A_STAGES = TILE_M <= 128 ? 8 : 5;
   static constexpr int ACT_OFF = 0;
-  static constexpr int W_OFF = ACT_OFF + STAGES * ACT_BYTES;
-  static constexpr int S_OFF = W_OFF + STAGES * WBLOCK_BYTES;
-  static constexpr int BAR_OFF = S_OFF + STAGES * SCALE_BYTES;
-  // barriers: full, empty (STAGES each), wfull, wempty (W_STAGES each),
-  // afull, aempty (2 each), drain (1)
-  static constexpr int NUM_BARS = 2 * STAGES + 2 * W_STAGES + 4 + 1;
+  static constexpr int W_OFF = ACT_OFF + A_STAGES * ACT_BYTES;
+  static constexpr int BAR_OFF = W_OFF + W_STAGES * W_SLOT;
+  static constexpr int NUM_BARS = 2 * A_STAGES + 2 * W_STAGES + 2 * T_STAGES + 2 * ACC + 1;
   static constexpr int MISC_OFF = BAR_OFF + NUM_BARS * 8;
   static constexpr int TOTAL = MISC_OFF + 16;
   static constexpr int DYN_BYTES = TOTAL + 1024;  // slack for 1024-byte alignment
   static_assert(ACT_BYTES % 1024 == 0, "activation stage must keep 1024B alignment");
-  static_assert(2 * TILE_M + ACC_COL0 <= TMEM_COLS, "TMEM budget");
+  static_assert(ACC_COL0 + ACC * TILE_M <= TMEM_COLS, "TMEM budget");
+  static_assert(DYN_BYTES <= 232448, "shared memory budget");
+  static_assert(T_STAGES % DEQ_GROUPS == 0 && W_STAGES % DEQ_GROUPS == 0, "stage ownership");
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mt, int& nt) {
@@ -77,31 +88,67 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
   nt = within / band_m;
 }
 
+// Convert 32 fp32 accumulator columns of one lane into 16 packed halves.
+__device__ __forceinline__ void pack_half2(const uint32_t* v, uint32_t* out, int n) {
+#pragma unroll
+  for (int j = 0; j < n; ++j) {
+    const __half2 h = __floats2half2_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+    out[j] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+}
+
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_wait16(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+               :
+               : "memory");
+}
+
 template <int TILE_M, int GROUP, bool FP32_OUT>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap act_map,
                    const uint8_t* __restrict__ tiles, const __half* __restrict__ scales,
                    void* __restrict__ c_out, int M, int N, int K, int* status,
                    unsigned long long wait_limit_ns) {
-  using L = Smem<TILE_M>;
-  constexpr int STAGES = L::STAGES;
+  using L = Cfg<TILE_M>;
+  constexpr int A_STAGES = L::A_STAGES;
+  constexpr int ACC = L::ACC;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
 
   const uint32_t act_base = smem_u32(smem + L::ACT_OFF);
   const uint32_t w_base = smem_u32(smem + L::W_OFF);
-  const uint32_t s_base = smem_u32(smem + L::S_OFF);
   const uint32_t bar_base = smem_u32(smem + L::BAR_OFF);
-  auto full_bar = [&](int s) { return bar_base + 8u * s; };
-  auto empty_bar = [&](int s) { return bar_base + 8u * (STAGES + s); };
-  auto wfull_bar = [&](int w) { return bar_base + 8u * (2 * STAGES + w); };
-  auto wempty_bar = [&](int w) { return bar_base + 8u * (2 * STAGES + W_STAGES + w); };
-  auto afull_bar = [&](int a) { return bar_base + 8u * (2 * STAGES + 2 * W_STAGES + a); };
-  auto aempty_bar = [&](int a) {
-    return bar_base + 8u * (2 * STAGES + 2 * W_STAGES + 2 + a);
+  // barrier order: afull, aempty, wfull, wempty, tfull, tempty, dfull, dempty, drain
+  auto afull = [&](int i) { return bar_base + 8u * i; };
+  auto aempty = [&](int i) { return bar_base + 8u * (A_STAGES + i); };
+  auto wfull = [&](int i) { return bar_base + 8u * (2 * A_STAGES + i); };
+  auto wempty = [&](int i) { return bar_base + 8u * (2 * A_STAGES + W_STAGES + i); };
+  auto tfull = [&](int i) { return bar_base + 8u * (2 * A_STAGES + 2 * W_STAGES + i); };
+  auto tempty = [&](int i) {
+    return bar_base + 8u * (2 * A_STAGES + 2 * W_STAGES + T_STAGES + i);
   };
-  const uint32_t drain_bar = bar_base + 8u * (2 * STAGES + 2 * W_STAGES + 4);
+  auto dfull = [&](int i) {
+    return bar_base + 8u * (2 * A_STAGES + 2 * W_STAGES + 2 * T_STAGES + i);
+  };
+  auto dempty = [&](int i) {
+    return bar_base + 8u * (2 * A_STAGES + 2 * W_STAGES + 2 * T_STAGES + ACC + i);
+  };
+  const uint32_t drain_bar = bar_base + 8u * (L::NUM_BARS - 1);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC_OFF + 4);
 
@@ -114,17 +161,21 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int groups = K / GROUP;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(full_bar(s), 1);
-      mbar_init(empty_bar(s), 1 + NUM_DEQ_WARPS);
+    for (int i = 0; i < A_STAGES; ++i) {
+      mbar_init(afull(i), 1);
+      mbar_init(aempty(i), 1);  // MMA completion
     }
-    for (int w = 0; w < W_STAGES; ++w) {
-      mbar_init(wfull_bar(w), NUM_DEQ_WARPS * 32);
-      mbar_init(wempty_bar(w), 1);
+    for (int i = 0; i < W_STAGES; ++i) {
+      mbar_init(wfull(i), 1);
+      mbar_init(wempty(i), 4);  // the four warps of the dequant group that read it
     }
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(afull_bar(a), 1);
-      mbar_init(aempty_bar(a), NUM_EPI_WARPS * 32);
+    for (int i = 0; i < T_STAGES; ++i) {
+      mbar_init(tfull(i), 4 * 32);
+      mbar_init(tempty(i), 1);  // MMA completion
+    }
+    for (int i = 0; i < ACC; ++i) {
+      mbar_init(dfull(i), 1);
+      mbar_init(dempty(i), NUM_EPI_WARPS * 32);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -142,11 +193,41 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
+    // ------------------------------------------------- activation producer
     if (lane == 0) {
       uint32_t it = 0;
-      int last_issue[16];
-      for (int s = 0; s < STAGES; ++s) last_issue[s] = -1;
+      int last_issue[A_STAGES];
+      for (int s = 0; s < A_STAGES; ++s) last_issue[s] = -1;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int mt, nt;
+        tile_coords(tile, num_m, num_n, mt, nt);
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % A_STAGES;
+          const uint32_t ph = (it / A_STAGES) & 1u;
+          if (!mbar_wait(aempty(s), ph ^ 1u, abort_flag, status, wait_limit_ns)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(afull(s), L::ACT_BYTES);
+          tma_load_2d(act_base + s * L::ACT_BYTES, &act_map, afull(s), kb * BK, mt * TILE_M);
+          last_issue[s] = static_cast<int>(it);
+        }
+      }
+      if (!ok) {  // let every copy already issued land before the CTA exits
+        volatile int never = 0;
+        for (int s = 0; s < A_STAGES; ++s)
+          if (last_issue[s] >= 0)
+            mbar_wait(afull(s), (static_cast<uint32_t>(last_issue[s]) / A_STAGES) & 1u, &never,
+                      nullptr, 100000000ull);
+      }
+    }
+  } else if (warp == 2) {
+    // ----------------------------------------------------- weight producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      int last_issue[W_STAGES];
+      for (int s = 0; s < W_STAGES; ++s) last_issue[s] = -1;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         int mt, nt;
@@ -154,9 +235,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint8_t* wblk = tiles + static_cast<size_t>(nt) * kblocks * WBLOCK_BYTES;
         const __half* sblk = scales + static_cast<size_t>(nt) * groups * TILE_N;
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
-          const int s = it % STAGES;
-          const uint32_t ph = (it / STAGES) & 1u;
-          if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, status, wait_limit_ns)) {
+          const int s = it % W_STAGES;
+          const uint32_t ph = (it / W_STAGES) & 1u;
+          if (!mbar_wait(wempty(s), ph ^ 1u, abort_flag, status, wait_limit_ns)) {
             ok = false;
             break;
           }
@@ -164,23 +245,20 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (GROUP == 32) { g0 = 2 * kb; sbytes = 512; }
           else if (GROUP == 64) { g0 = kb; sbytes = 256; }
           else { g0 = kb >> 1; sbytes = 256; }
-          mbar_arrive_expect_tx(full_bar(s), L::ACT_BYTES + WBLOCK_BYTES + sbytes);
-          tma_load_2d(act_base + s * L::ACT_BYTES, &act_map, full_bar(s), kb * BK, mt * TILE_M);
-          bulk_load(w_base + s * WBLOCK_BYTES, wblk + static_cast<size_t>(kb) * WBLOCK_BYTES,
-                    WBLOCK_BYTES, full_bar(s));
-          bulk_load(s_base + s * SCALE_BYTES, sblk + static_cast<size_t>(g0) * TILE_N, sbytes,
-                    full_bar(s));
+          mbar_arrive_expect_tx(wfull(s), WBLOCK_BYTES + sbytes);
+          bulk_load(w_base + s * W_SLOT, wblk + static_cast<size_t>(kb) * WBLOCK_BYTES,
+                    WBLOCK_BYTES, wfull(s));
+          bulk_load(w_base + s * W_SLOT + WBLOCK_BYTES, sblk + static_cast<size_t>(g0) * TILE_N,
+                    sbytes, wfull(s));
           last_issue[s] = static_cast<int>(it);
         }
       }
       if (!ok) {
-        // Let every copy already issued land before the CTA exits.
-        for (int s = 0; s < STAGES; ++s)
-          if (last_issue[s] >= 0) {
-            volatile int never = 0;
-            mbar_wait(full_bar(s), (static_cast<uint32_t>(last_issue[s]) / STAGES) & 1u, &never,
+        volatile int never = 0;
+        for (int s = 0; s < W_STAGES; ++s)
+          if (last_issue[s] >= 0)
+            mbar_wait(wfull(s), (static_cast<uint32_t>(last_issue[s]) / W_STAGES) & 1u, &never,
                       nullptr, 100000000ull);
-          }
       }
     }
   } else if (warp == 1) {
@@ -190,21 +268,21 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t it = 0, t_local = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++t_local) {
-        const int acc = t_local & 1;
-        const uint32_t aph = (t_local >> 1) & 1u;
-        if (!mbar_wait(aempty_bar(acc), aph ^ 1u, abort_flag, status, wait_limit_ns)) {
+        const int acc = t_local % ACC;
+        const uint32_t dph = (t_local / ACC) & 1u;
+        if (!mbar_wait(dempty(acc), dph ^ 1u, abort_flag, status, wait_limit_ns)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + ACC_COL0 + acc * TILE_M;
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
-          const int s = it % STAGES;
-          const uint32_t ph = (it / STAGES) & 1u;
-          const int ws = it % W_STAGES;
-          const uint32_t wph = (it / W_STAGES) & 1u;
-          if (!mbar_wait(full_bar(s), ph, abort_flag, status, wait_limit_ns) ||
-              !mbar_wait(wfull_bar(ws), wph, abort_flag, status, wait_limit_ns)) {
+          const int s = it % A_STAGES;
+          const uint32_t ph = (it / A_STAGES) & 1u;
+          const int ts = it % T_STAGES;
+          const uint32_t tph = (it / T_STAGES) & 1u;
+          if (!mbar_wait(afull(s), ph, abort_flag, status, wait_limit_ns) ||
+              !mbar_wait(tfull(ts), tph, abort_flag, status, wait_limit_ns)) {
             ok = false;
             break;
           }
@@ -212,106 +290,142 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t b_addr = act_base + s * L::ACT_BYTES;
 #pragma unroll
           for (int k16 = 0; k16 < BK / 16; ++k16) {
-            const uint32_t a_tmem = tmem_base + ws * W_COLS + k16 * 8;
+            const uint32_t a_tmem = tmem_base + ts * T_COLS + k16 * 8;
             const uint64_t b_desc = smem_desc_sw128(b_addr + k16 * 32);
             mma_f16_ts(d_tmem, a_tmem, b_desc, IDESC, (kb | k16) != 0);
           }
-          tc_commit(empty_bar(s));
-          tc_commit(wempty_bar(ws));
+          tc_commit(aempty(s));
+          tc_commit(tempty(ts));
         }
         if (!ok) break;
-        tc_commit(afull_bar(acc));
+        tc_commit(dfull(acc));
       }
-      // Drain: every MMA this thread issued has completed before TMEM is freed.
+      // Every MMA this thread issued has completed before TMEM is freed.
       tc_commit(drain_bar);
       volatile int never = 0;
       mbar_wait(drain_bar, 0, &never, nullptr, 100000000ull);
     }
-  } else if (warp < 2 + NUM_DEQ_WARPS) {
+  } else if (warp < FIRST_EPI_WARP) {
     // ---------------------------------------------------------------- dequant
-    const int d = warp - 2;
+    const int dgroup = (warp - FIRST_DEQ_WARP) >> 2;
     const int quarter = warp & 3;          // TMEM lanes this warp may access
-    const int h = d / 4;                   // which 32 of the 64 k in a stage
     const int row = quarter * 32 + lane;   // weight column inside the tile
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-    uint32_t it = 0;
-    bool ok = true;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      for (int kb = 0; kb < kblocks; ++kb, ++it) {
-        const int s = it % STAGES;
-        const uint32_t ph = (it / STAGES) & 1u;
-        const int ws = it % W_STAGES;
-        const uint32_t wph = (it / W_STAGES) & 1u;
-        if (!mbar_wait(full_bar(s), ph, abort_flag, status, wait_limit_ns)) {
-          ok = false;
-          break;
-        }
-        uint4 codes;
-        asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-                     : "=r"(codes.x), "=r"(codes.y), "=r"(codes.z), "=r"(codes.w)
-                     : "r"(w_base + s * WBLOCK_BYTES + h * 2048 + row * 16));
-        const int gl = (GROUP == 32) ? h : 0;
-        uint16_t sbits;
-        asm volatile("ld.shared.u16 %0, [%1];"
-                     : "=h"(sbits)
-                     : "r"(s_base + s * SCALE_BYTES + (gl * TILE_N + row) * 2));
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty_bar(s));
-        const uint32_t s2 = half_bits_x2(sbits);
-        uint32_t r[16];
-        const uint32_t wv[4] = {codes.x, codes.y, codes.z, codes.w};
+    uint32_t it = static_cast<uint32_t>(dgroup);
+    const uint32_t total = static_cast<uint32_t>(kblocks) *
+                           static_cast<uint32_t>((num_tiles - static_cast<int>(blockIdx.x) +
+                                                  static_cast<int>(gridDim.x) - 1) /
+                                                 static_cast<int>(gridDim.x));
+    for (; it < total; it += DEQ_GROUPS) {
+      const int s = it % W_STAGES;
+      const uint32_t ph = (it / W_STAGES) & 1u;
+      const int ts = it % T_STAGES;
+      const uint32_t tph = (it / T_STAGES) & 1u;
+      if (!mbar_wait(wfull(s), ph, abort_flag, status, wait_limit_ns)) break;
+      const uint32_t wsrc = w_base + s * W_SLOT + row * 16;
+      uint4 c0, c1;
+      asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(c0.x), "=r"(c0.y), "=r"(c0.z), "=r"(c0.w)
+                   : "r"(wsrc));
+      asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(c1.x), "=r"(c1.y), "=r"(c1.z), "=r"(c1.w)
+                   : "r"(wsrc + 2048));
+      uint16_t sb0, sb1;
+      const uint32_t ssrc = w_base + s * W_SLOT + WBLOCK_BYTES + row * 2;
+      asm volatile("ld.shared.u16 %0, [%1];" : "=h"(sb0) : "r"(ssrc));
+      if (GROUP == 32)
+        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(sb1) : "r"(ssrc + TILE_N * 2));
+      else
+        sb1 = sb0;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(wempty(s));
+      const uint32_t s0 = half_bits_x2(sb0), s1 = half_bits_x2(sb1);
+      uint32_t r[32];
+      const uint32_t wv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          r[4 * i + 0] = decode_pair<0>(wv[i], s2);
-          r[4 * i + 1] = decode_pair<1>(wv[i], s2);
-          r[4 * i + 2] = decode_pair<2>(wv[i], s2);
-          r[4 * i + 3] = decode_pair<3>(wv[i], s2);
-        }
-        if (!mbar_wait(wempty_bar(ws), wph ^ 1u, abort_flag, status, wait_limit_ns)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        tmem_st_32x32b_x16(tmem_base + lane_addr + ws * W_COLS + h * 16, r);
-        tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive(wfull_bar(ws));
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t sc = i < 4 ? s0 : s1;
+        r[4 * i + 0] = decode_pair<0>(wv[i], sc);
+        r[4 * i + 1] = decode_pair<1>(wv[i], sc);
+        r[4 * i + 2] = decode_pair<2>(wv[i], sc);
+        r[4 * i + 3] = decode_pair<3>(wv[i], sc);
       }
+      if (!mbar_wait(tempty(ts), tph ^ 1u, abort_flag, status, wait_limit_ns)) break;
+      tc_fence_after();
+      tmem_st_32x32b_x32(tmem_base + lane_addr + ts * T_COLS, r);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(tfull(ts));
     }
   } else {
     // --------------------------------------------------------------- epilogue
+    // Four warps per lane quarter; warp e covers accumulator columns
+    // [part*TILE_M/4, (part+1)*TILE_M/4) of its 32 lanes. The whole slice is
+    // read into registers before the accumulator is released, so the next
+    // tile's MMAs start while the stores drain.
+    constexpr int COLS = TILE_M / 4;
+    const int e = warp - FIRST_EPI_WARP;
     const int quarter = warp & 3;
+    const int half = e >> 2;  // which quarter of the columns
     const int row = quarter * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     uint32_t t_local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t_local) {
       int mt, nt;
       tile_coords(tile, num_m, num_n, mt, nt);
-      const int acc = t_local & 1;
-      const uint32_t aph = (t_local >> 1) & 1u;
-      if (!mbar_wait(afull_bar(acc), aph, abort_flag, status, wait_limit_ns)) break;
+      const int acc = t_local % ACC;
+      const uint32_t dph = (t_local / ACC) & 1u;
+      if (!mbar_wait(dfull(acc), dph, abort_flag, status, wait_limit_ns)) break;
       tc_fence_after();
+      const uint32_t col0 = tmem_base + lane_addr + ACC_COL0 + acc * TILE_M + half * COLS;
       const int n = nt * TILE_N + row;
+      const int m0 = mt * TILE_M + half * COLS;
+      if constexpr (FP32_OUT) {
+        // FP32 C: store each 16-column chunk as it is read.
+        float* cp = static_cast<float*>(c_out) + static_cast<size_t>(m0) * N + n;
 #pragma unroll 1
-      for (int c = 0; c < TILE_M / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem_base + lane_addr + ACC_COL0 + acc * TILE_M + c * 32, v);
-        tmem_ld_wait(v);
-        const int m0 = mt * TILE_M + c * 32;
-        if constexpr (FP32_OUT) {
-          float* cp = static_cast<float*>(c_out) + static_cast<size_t>(m0) * N + n;
+        for (int c = 0; c < COLS / 16; ++c) {
+          uint32_t v[16];
+          tmem_ld_32x32b_x16(col0 + c * 16, v);
+          tmem_ld_wait16(v);
+          if (c == COLS / 16 - 1) {
+            tc_fence_before();
+            mbar_arrive(dempty(acc));
+          }
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (m0 + j < M) cp[static_cast<size_t>(j) * N] = __uint_as_float(v[j]);
+          for (int j = 0; j < 16; ++j)
+            if (m0 + c * 16 + j < M)
+              cp[static_cast<size_t>(c * 16 + j) * N] = __uint_as_float(v[j]);
+        }
+      } else {
+        uint32_t h[COLS / 2];  // packed halves: h[j] = columns 2j, 2j+1
+#pragma unroll
+        for (int c = 0; c < COLS / 16; ++c) {
+          uint32_t v[16];
+          tmem_ld_32x32b_x16(col0 + c * 16, v);
+          tmem_ld_wait16(v);
+          pack_half2(v, &h[c * 8], 8);
+        }
+        tc_fence_before();
+        mbar_arrive(dempty(acc));
+        __half* cp = static_cast<__half*>(c_out) + static_cast<size_t>(m0) * N + n;
+        const int valid = min(COLS, M - m0);
+        if (valid >= COLS) {
+#pragma unroll
+          for (int j = 0; j < COLS / 2; ++j) {
+            const __half2 hv = *reinterpret_cast<const __half2*>(&h[j]);
+            cp[static_cast<size_t>(2 * j) * N] = __low2half(hv);
+            cp[static_cast<size_t>(2 * j + 1) * N] = __high2half(hv);
+          }
         } else {
-          __half* cp = static_cast<__half*>(c_out) + static_cast<size_t>(m0) * N + n;
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (m0 + j < M) cp[static_cast<size_t>(j) * N] = __float2half_rn(__uint_as_float(v[j]));
+          for (int j = 0; j < COLS / 2; ++j) {
+            const __half2 hv = *reinterpret_cast<const __half2*>(&h[j]);
+            if (2 * j < valid) cp[static_cast<size_t>(2 * j) * N] = __low2half(hv);
+            if (2 * j + 1 < valid) cp[static_cast<size_t>(2 * j + 1) * N] = __high2half(hv);
+          }
         }
       }
-      tc_fence_before();
-      mbar_arrive(aempty_bar(acc));
     }
   }
 
@@ -330,7 +444,7 @@ template <int TILE_M, int GROUP, bool FP32_OUT>
 cudaError_t launch_impl(const CUtensorMap& act_map, const uint8_t* tiles, const __half* scales,
                         void* c, int M, int N, int K, int sm_count, int* status,
                         unsigned long long wait_limit_ns, cudaStream_t stream) {
-  using L = Smem<TILE_M>;
+  using L = Cfg<TILE_M>;
   auto kernel = gemm_tc_kernel<TILE_M, GROUP, FP32_OUT>;
   static bool configured = false;  // per instantiation; idempotent attribute
   if (!configured) {
@@ -365,22 +479,11 @@ cudaError_t launch_group(const CUtensorMap& act_map, const uint8_t* tiles,
 }
 
 int choose_tile_m(int M, int N, int sm_count) {
-  // Estimated main-loop time ~ waves x per-tile cost; per-tile cost grows
-  // with TILE_M, with a floor for the fixed dequant work of a weight block.
-  static const int options[3] = {64, 128, 192};
-  int best = 192;
-  double best_cost = 1e30;
-  for (int tm : options) {
-    const long tiles = static_cast<long>((M + tm - 1) / tm) * (N / TILE_N);
-    const long waves = (tiles + sm_count - 1) / sm_count;
-    const double per_tile = tm > 96 ? tm : 96.0;
-    const double cost = static_cast<double>(waves) * per_tile;
-    if (cost < best_cost - 1e-9) {
-      best_cost = cost;
-      best = tm;
-    }
-  }
-  return best;
+  // A 128 x N x 16 MMA costs about the same for any N <= 256, so N = 256
+  // wins unless the activation rows (M) do not fill it.
+  (void)N;
+  (void)sm_count;
+  return M <= 128 ? 128 : 256;
 }
 
 cudaError_t launch(const CUtensorMap& act_map, int tile_m, const uint8_t* tiles,
@@ -393,9 +496,8 @@ cudaError_t launch(const CUtensorMap& act_map, int tile_m, const uint8_t* tiles,
                                              sm_count, status, wait_limit_ns, stream)         \
                     : launch_group<TM, false>(act_map, tiles, scales, c, M, N, K, group,      \
                                               sm_count, status, wait_limit_ns, stream);
-  I4G_TC_CASE(64)
   I4G_TC_CASE(128)
-  I4G_TC_CASE(192)
+  I4G_TC_CASE(256)
 #undef I4G_TC_CASE
   return cudaErrorInvalidValue;
 }

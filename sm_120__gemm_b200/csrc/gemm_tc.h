@@ -19,7 +19,7 @@ cudaError_t launch(const CUtensorMap& act_map, int tile_m, const uint8_t* tiles,
 namespace dec {
 constexpr int MAX_M = 16;
 cudaError_t launch(const __half* a, const uint8_t* tiles, const __half* scales, __half* c,
-                   int M, int N, int K, int group, cudaStream_t stream);
+                   int M, int N, int K, int group, int sm_count, cudaStream_t stream);
 }  // namespace dec
 
 namespace prep {
