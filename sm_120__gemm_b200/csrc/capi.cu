@@ -123,46 +123,71 @@ int encode_fn(EncodeTiledFn* out) {
   return I4G_OK;
 }
 
-// Activation map: A [M][K] fp16, box 64 (K) x tile_m (M) rows, 128-byte
-// swizzle, zero fill past M. Cached per host thread and key, as the
-// reference caches its maps (kernels/gemm_v17_instruction.cu:214-228).
-struct ActMapCache {
+// Activation map of A [M][K] fp16, 128-byte swizzle, zero fill past M:
+// rows > 0 gives the 2-D box 64 (K) x rows (M); rows < 0 the 3-D box of
+// four consecutive 64-k blocks x -rows rows. A few recent maps are cached per host thread, keyed by
+// pointer and shape, as the reference caches its maps
+// (kernels/gemm_v17_instruction.cu:214-228).
+struct ActMapEntry {
   int device = -1;
   const void* a = nullptr;
-  int M = 0, K = 0, tile_m = 0;
+  int M = 0, K = 0, rows = 0;
+  unsigned long long used = 0;
   CUtensorMap map;
 };
 
-int act_map(const void* A, int M, int K, int tile_m, const CUtensorMap** out) {
-  thread_local ActMapCache cache;
+int act_map(const void* A, int M, int K, int rows, const CUtensorMap** out) {
+  constexpr int kEntries = 8;
+  thread_local ActMapEntry cache[kEntries];
+  thread_local unsigned long long clock = 0;
   int dev = -1;
   cudaGetDevice(&dev);
-  if (cache.device == dev && cache.a == A && cache.M == M && cache.K == K &&
-      cache.tile_m == tile_m) {
-    *out = &cache.map;
-    return I4G_OK;
+  ++clock;
+  ActMapEntry* victim = &cache[0];
+  for (ActMapEntry& e : cache) {
+    if (e.device == dev && e.a == A && e.M == M && e.K == K && e.rows == rows) {
+      e.used = clock;
+      *out = &e.map;
+      return I4G_OK;
+    }
+    if (e.used < victim->used) victim = &e;
   }
   EncodeTiledFn encode = nullptr;
   int st = encode_fn(&encode);
   if (st != I4G_OK) return st;
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
-  const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(tile_m)};
-  const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = encode(&cache.map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(A),
-                            dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r;
+  if (rows > 0) {
+    // 2-D view [M][K]: box of 64 k x `rows` rows (the tcgen05 kernel)
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
+    const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(rows)};
+    const cuuint32_t estr[2] = {1, 1};
+    r = encode(&victim->map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(A), dims,
+               strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    // 3-D view {64 k, M rows, K/64 blocks}: box of 64 k x -rows rows x 4
+    // blocks (the decode kernel's ring stage)
+    const cuuint64_t dims[3] = {64, static_cast<cuuint64_t>(M), static_cast<cuuint64_t>(K / 64)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(K) * 2, 128};
+    const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(-rows), 4};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    r = encode(&victim->map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(A), dims,
+               strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
   if (r != CUDA_SUCCESS) {
-    cache.device = -1;
+    victim->device = -1;
+    victim->used = 0;
     return fail(I4G_ERR_DRIVER, "cuTensorMapEncodeTiled failed with CUresult %d", int(r));
   }
-  cache.device = dev;
-  cache.a = A;
-  cache.M = M;
-  cache.K = K;
-  cache.tile_m = tile_m;
-  *out = &cache.map;
+  victim->device = dev;
+  victim->a = A;
+  victim->M = M;
+  victim->K = K;
+  victim->rows = rows;
+  victim->used = clock;
+  *out = &victim->map;
   return I4G_OK;
 }
 
@@ -204,10 +229,14 @@ int gemm_common(const void* A, const uint8_t* tiles, const void* scales, void* C
   if (st != I4G_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const __half* sc = static_cast<const __half*>(scales);
-  if (variant == I4G_VARIANT_DECODE)
-    return finish(i4g::dec::launch(static_cast<const __half*>(A), tiles, sc,
-                                   static_cast<__half*>(C), M, N, K, group, dev->sm_count, s),
+  if (variant == I4G_VARIANT_DECODE) {
+    const CUtensorMap* dmap = nullptr;
+    st = act_map(A, M, K, -i4g::dec::rows_for(M), &dmap);
+    if (st != I4G_OK) return st;
+    return finish(i4g::dec::launch(*dmap, tiles, sc, static_cast<__half*>(C), M, N, K, group,
+                                   dev->sm_count, dev->status_word, g_wait_limit_ns, s),
                   "decode kernel launch");
+  }
   const int tile_m = tile_m_override() ? tile_m_override()
                                        : i4g::tc::choose_tile_m(M, N, dev->sm_count);
   const CUtensorMap* map = nullptr;

@@ -281,8 +281,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t ph = (it / A_STAGES) & 1u;
           const int ts = it % T_STAGES;
           const uint32_t tph = (it / T_STAGES) & 1u;
-          if (!mbar_wait(afull(s), ph, abort_flag, status, wait_limit_ns) ||
-              !mbar_wait(tfull(ts), tph, abort_flag, status, wait_limit_ns)) {
+          if (!mbar_wait_lean(afull(s), ph, abort_flag, status, wait_limit_ns) ||
+              !mbar_wait_lean(tfull(ts), tph, abort_flag, status, wait_limit_ns)) {
             ok = false;
             break;
           }

@@ -18,8 +18,11 @@ cudaError_t launch(const CUtensorMap& act_map, int tile_m, const uint8_t* tiles,
 
 namespace dec {
 constexpr int MAX_M = 16;
-cudaError_t launch(const __half* a, const uint8_t* tiles, const __half* scales, __half* c,
-                   int M, int N, int K, int group, int sm_count, cudaStream_t stream);
+// Rows of the activation box the decode kernel's tensor map must use.
+int rows_for(int M);
+cudaError_t launch(const CUtensorMap& act_map, const uint8_t* tiles, const __half* scales,
+                   __half* c, int M, int N, int K, int group, int sm_count, int* status,
+                   unsigned long long wait_limit_ns, cudaStream_t stream);
 }  // namespace dec
 
 namespace prep {

@@ -6,6 +6,7 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cstdint>
+#include <cstring>
 
 namespace i4g {
 
@@ -48,6 +49,22 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
                : "memory");
 }
 
+// try_wait that may suspend the thread for up to `hint_ns` while the phase is
+// incomplete (the hardware resumes it as soon as the phase completes), so a
+// waiting warp does not spend issue slots polling.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity,
+                                                    uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -60,19 +77,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Wait for the phase of `bar` with the given parity. Gives up (returns
-// false) when *abort is set by another warp, or after `limit_ns` of
-// waiting, in which case it sets *abort and records a timeout in *status.
-// Every spin in the kernels goes through here, so no wait is unbounded.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
-                                          volatile int* abort, int* status,
-                                          uint64_t limit_ns) {
-  if (mbar_try_wait(bar, parity)) return true;
+// Slow path of mbar_wait: keep polling until the phase completes, *abort is
+// set by another warp, or `limit_ns` passes (then sets *abort and records a
+// timeout in *status). Out of line so the common, already-complete case
+// costs one try_wait.
+static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, volatile int* abort,
+                                            int* status, uint64_t limit_ns) {
   const uint64_t t0 = global_timer_ns();
   while (true) {
 #pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
+    for (int i = 0; i < 8; ++i)
+      if (mbar_try_wait_sleep(bar, parity, 20000)) return true;
     if (*abort) return false;
     if (global_timer_ns() - t0 > limit_ns) {
       *abort = 1;
@@ -80,6 +95,37 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
       return false;
     }
   }
+}
+
+// Wait for the phase of `bar` with the given parity. Gives up (returns
+// false) when *abort is set by another warp, or after `limit_ns` of
+// waiting. Every spin in the kernels goes through here or mbar_wait_lean,
+// so no wait is unbounded.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
+                                          volatile int* abort, int* status,
+                                          uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 8; ++i)
+      if (mbar_try_wait_sleep(bar, parity, 20000)) return true;
+    if (*abort) return false;
+    if (global_timer_ns() - t0 > limit_ns) {
+      *abort = 1;
+      if (status) atomicExch(status, kStatusTimeout);
+      return false;
+    }
+  }
+}
+
+// mbar_wait with the polling loop out of line, for the MMA-issuing thread,
+// whose per-block bookkeeping sits between tensor-core instructions.
+__device__ __forceinline__ bool mbar_wait_lean(uint32_t bar, uint32_t parity,
+                                               volatile int* abort, int* status,
+                                               uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, abort, status, limit_ns);
 }
 
 // ------------------------------------------------------------ TMA / bulk
@@ -96,6 +142,16 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* map, uint3
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
       "l"(map), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+
+// 3-D tiled TMA load, no multicast.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* map, uint32_t bar,
+                                            int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(map), "r"(bar), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
 
@@ -236,34 +292,32 @@ __device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
 
 // ---------------------------------------------------- INT4 -> FP16 decode
 
-__device__ __forceinline__ uint32_t lop3_and_xor(uint32_t a, uint32_t b, uint32_t c) {
-  uint32_t d;  // (a & b) ^ c
-  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
+__device__ __forceinline__ __half2 u32_as_half2(uint32_t v) {
+  __half2 h;
+  static_assert(sizeof(h) == sizeof(v), "half2 is 32 bits");
+  memcpy(&h, &v, sizeof(v));
+  return h;
 }
 
-__device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-
-__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
+__device__ __forceinline__ uint32_t half2_as_u32(__half2 h) {
+  uint32_t v;
+  memcpy(&v, &h, sizeof(v));
+  return v;
 }
 
 // Decode pair p (0..3) of a tile-layout word into half2 {half(q0*s), half(q1*s)}.
 // The nibble pair sits at bits [4p, 4p+4) and [16+4p, 20+4p). (nib & 15) ^ 8
 // ORed into 0x6400 is the half 1024 + 8 + q, so one exact subtraction of 1032
-// gives q, and one RN multiply gives half(q * s): the value the reference's
-// dequantize computes as __float2half(float(q) * float(s)).
+// gives q, and one round-to-nearest multiply gives half(q * s): the value the
+// reference's dequantize computes as __float2half(float(q) * float(s)).
+// Written in C++ (not inline PTX) so the compiler keeps the constants in
+// immediates or hoisted registers.
 template <int P>
 __device__ __forceinline__ uint32_t decode_pair(uint32_t word, uint32_t scale2) {
   const uint32_t x = (P == 0) ? word : (word >> (4 * P));
-  const uint32_t biased = lop3_and_xor(x, 0x000F000Fu, 0x64086408u);
-  return hmul2_u32(hsub2_u32(biased, 0x64086408u), scale2);
+  const uint32_t biased = (x & 0x000F000Fu) ^ 0x64086408u;
+  const __half2 q = __hsub2(u32_as_half2(biased), u32_as_half2(0x64086408u));
+  return half2_as_u32(__hmul2(q, u32_as_half2(scale2)));
 }
 
 __device__ __forceinline__ uint32_t half_bits_x2(uint16_t h) {
