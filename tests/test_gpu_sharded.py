@@ -1,0 +1,73 @@
+"""Column-parallel GEMM over NCCL on 2+ GPUs (skips on a single-GPU box).
+
+Each rank quantizes the same seeded weight, keeps its column slice (a view
+into the tile and scale layouts), runs the fused GEMM on it and all-gathers
+the FP16 column blocks; the gathered C must equal the single-GPU C bit for bit
+(every output column is computed by the same kernel in the same k order)."""
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q, M, N, K, group):
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import torch.distributed as dist
+
+    import sm_120__gemm_b200 as i4g
+    from sm_120__gemm_b200.sharded import ColumnParallelLinear
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        g = torch.Generator().manual_seed(77)
+        w = (torch.randn(K, N, generator=g) * 0.02).half().cuda()
+        a = (torch.rand(M, K, generator=g) * 2 - 1).half().cuda()
+        full = i4g.QuantizedLinear.from_weight(w, group)
+        cp = ColumnParallelLinear.from_full(full)
+        c = cp.forward(a, gather=True)
+        torch.cuda.synchronize()
+        if rank == 0:
+            ref = full(a)
+            torch.cuda.synchronize()
+            q.put(bool(torch.equal(c.view(torch.int16), ref.view(torch.int16))))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("M,N,K,group", [(512, 1024, 1024, 64), (8, 2048, 2048, 128),
+                                         (300, 4096, 512, 32)])
+def test_column_parallel_matches_single_gpu(M, N, K, group):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    world = min(torch.cuda.device_count(), 4)
+    while N % (128 * world):
+        world -= 1
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, M, N, K, group))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+        assert p.exitcode == 0
+    assert q.get(timeout=10) is True
