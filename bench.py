@@ -159,6 +159,8 @@ def run_ours(args, rank, world, local_rank):
     acts = [(torch.rand(M, K, generator=gen_a, device=dev) * 2 - 1).half() for _ in range(n_act)]
     lins = {g: [weights(g, r) for r in range(n_wset)] for g in GROUPS}
     outs = [torch.empty(M, n_local, dtype=torch.float16, device=dev) for _ in range(3)]
+    # Split-K workspace for the last partial wave (None: whole tiles only).
+    ws = i4g.workspace_for(M, n_local, K, dev, stream) if args.schedule == "split" else None
     torch.cuda.synchronize()
 
     def step(i, events=None):
@@ -167,7 +169,7 @@ def run_ours(args, rank, world, local_rank):
             a = acts[(3 * i + j) % n_act]
             if events is not None:
                 events[j][0].record(stream)
-            i4g.launch_final(a, lin.tiles, lin.scales, outs[j], M, n_local, K, g, stream)
+            i4g.launch_final_ws(a, lin.tiles, lin.scales, outs[j], M, n_local, K, g, ws, stream)
             if events is not None:
                 events[j][1].record(stream)
 
@@ -214,7 +216,9 @@ def run_ours(args, rank, world, local_rank):
         "data": "synthetic (seeded): A fp16 U[-1,1]; W fp32 N(0,0.02) -> fp16 -> INT4",
         "config": {"workload": WORKLOAD, "M": M, "N_per_gpu": n_local, "N_total": n_total,
                    "K": K, "groups": list(GROUPS), "parallelism": f"column-parallel x{world}",
-                   "l2": "rotating inputs: 4 x 32 MiB activations, 2 weight sets per group"},
+                   "l2": "rotating inputs: 4 x 32 MiB activations, 2 weight sets per group",
+                   "schedule": args.schedule + (f" (workspace {ws.numel()} B)" if ws is not None
+                                                else "")},
         "per_group": {str(g): {"kernel_ms": round(kernel_ms[g], 4),
                                "tflops": round(flops(M, n_local, K) / kernel_ms[g] / 1e9, 1)}
                       for g in GROUPS},
@@ -273,7 +277,7 @@ def run_e2e(args, i4g, lins, dev):
     return {"value": round(sum(flops(M, N, K) for _ in GROUPS) / (ms * 1e-3) / 1e12, 2),
             "unit": UNIT, "h2d_bytes_per_step": len(GROUPS) * M * K * 2,
             "d2h_bytes_per_step": len(GROUPS) * M * N * 2, "ms_per_step": round(ms, 4),
-            "path": "QuantizedLinear -> launch_final (C ABI i4g_gemm), pinned host A and C"}
+            "path": "QuantizedLinear -> launch_final_ws (C ABI i4g_gemm_ws), pinned host A and C"}
 
 
 def run_decode(args, i4g, dev, peaks):
@@ -435,6 +439,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-rows", type=int, default=64)
+    ap.add_argument("--schedule", choices=["split", "whole"], default="split",
+                    help="split: split-K the last partial wave through a workspace; "
+                         "whole: whole output tiles only (i4g_gemm)")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the e2e / decode / cpu-baseline legs")
     args = ap.parse_args()

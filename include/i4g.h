@@ -131,6 +131,32 @@ int i4g_gemm_variant(const void* A, const uint8_t* tiles, const void* scales,
                      void* C, int M, int N, int K, int group, int variant,
                      void* stream);
 
+/* ---- split-K workspace (no counterpart in the reference) ------------------ */
+
+/* The tcgen05 kernel runs ceil(M/TILE_M) x N/128 output tiles on one CTA per
+ * SM. When the tile count is not a multiple of the SM count, the *_ws entry
+ * points split the tiles of the last, partial wave along K (2 to 4 ways) and
+ * reduce their FP32 partial tiles through a caller-owned workspace, in a fixed
+ * order, so results are bitwise reproducible and within the usual FP32
+ * accumulation tolerance of the unsplit kernel.
+ *
+ * i4g_gemm_workspace_size: bytes needed for this shape on the current device
+ * (0 when nothing would be split, e.g. M <= 16 or a whole number of waves).
+ *
+ * i4g_gemm_ws / i4g_gemm_fp32_ws: i4g_gemm / i4g_gemm_fp32 with a workspace.
+ * workspace: 256-byte aligned device memory, ZEROED ONCE before its first use
+ * (its first 1024 bytes are arrival counters that every launch returns to
+ * zero). workspace == NULL or workspace_bytes smaller than needed runs the
+ * unsplit schedule. Launches sharing one workspace must be ordered (one
+ * stream); concurrent launches on the same workspace race. */
+int i4g_gemm_workspace_size(int M, int N, int K, size_t* bytes);
+int i4g_gemm_ws(const void* A, const uint8_t* tiles, const void* scales, void* C,
+                int M, int N, int K, int group, void* workspace,
+                size_t workspace_bytes, void* stream);
+int i4g_gemm_fp32_ws(const void* A, const uint8_t* tiles, const void* scales,
+                     float* C, int M, int N, int K, int group, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
 /* ---- column-parallel sharding --------------------------------------------- */
 
 /* Byte offsets of rank `rank`'s slice of a G-way column-parallel split of the

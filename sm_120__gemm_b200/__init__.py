@@ -61,6 +61,9 @@ _SIGNATURES = {
     "i4g_gemm": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp],
     "i4g_gemm_fp32": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp],
     "i4g_gemm_variant": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp],
+    "i4g_gemm_workspace_size": [_i, _i, _i, ctypes.POINTER(ctypes.c_size_t)],
+    "i4g_gemm_ws": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, ctypes.c_size_t, _vp],
+    "i4g_gemm_fp32_ws": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, ctypes.c_size_t, _vp],
     "i4g_shard_range": [_i, _i, _i, _i, _i, ctypes.POINTER(ctypes.c_size_t),
                         ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(_i),
                         ctypes.POINTER(_i)],
@@ -190,6 +193,52 @@ def launch_gemm_variant(a, b_repacked, scales_repacked, c, M: int, N: int, K: in
                         variant: int, stream=None) -> None:
     _call("i4g_gemm_variant", _ptr(a), _ptr(b_repacked), _ptr(scales_repacked), _ptr(c), M, N,
           K, group, variant, _stream(stream))
+
+
+def gemm_workspace_size(M: int, N: int, K: int) -> int:
+    """Bytes of split-K workspace the current device wants for this shape (0: none)."""
+    b = ctypes.c_size_t()
+    _call("i4g_gemm_workspace_size", M, N, K, ctypes.byref(b))
+    return b.value
+
+
+def launch_final_ws(a, b_repacked, scales_repacked, c, M: int, N: int, K: int, group: int,
+                    workspace, stream=None) -> None:
+    """launch_final with a split-K workspace: a zero-initialised uint8 CUDA
+    tensor (``workspace_for``); calls sharing it must be stream-ordered."""
+    _call("i4g_gemm_ws", _ptr(a), _ptr(b_repacked), _ptr(scales_repacked), _ptr(c), M, N, K,
+          group, _ptr(workspace), 0 if workspace is None else workspace.numel(),
+          _stream(stream))
+
+
+def launch_final_fp32_ws(a, b_repacked, scales_repacked, c, M: int, N: int, K: int,
+                         group: int, workspace, stream=None) -> None:
+    _call("i4g_gemm_fp32_ws", _ptr(a), _ptr(b_repacked), _ptr(scales_repacked), _ptr(c), M, N,
+          K, group, _ptr(workspace), 0 if workspace is None else workspace.numel(),
+          _stream(stream))
+
+
+_workspaces: dict = {}
+
+
+def workspace_for(M: int, N: int, K: int, device=None, stream=None):
+    """A zeroed split-K workspace for (device, stream), grown on demand.
+
+    One buffer per stream keeps launches that share it ordered. The kernel
+    leaves the workspace's counters at zero, so it is zeroed only when made.
+    Returns None when the shape needs no workspace."""
+    import torch
+    need = gemm_workspace_size(M, N, K)
+    if need == 0:
+        return None
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None \
+        else torch.device(device)
+    key = (dev.index, _stream(stream))
+    ws = _workspaces.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.zeros(need, dtype=torch.uint8, device=dev)
+        _workspaces[key] = ws
+    return ws
 
 
 def shard_range(K: int, N: int, group: int, world: int, rank: int):

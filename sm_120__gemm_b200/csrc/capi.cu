@@ -193,30 +193,45 @@ int act_map(const void* A, int M, int K, int rows, const CUtensorMap** out) {
 
 unsigned long long g_wait_limit_ns = kDefaultWaitLimitNs;
 
-// Tuning override for the tcgen05 kernel's activation tile (64, 128 or 192
+// Tuning override for the tcgen05 kernel's activation tile (128 or 256
 // rows), read once from I4G_TILE_M; 0 means the shape-based choice.
 int tile_m_override() {
   static const int v = [] {
     const char* e = std::getenv("I4G_TILE_M");
     const int t = e ? std::atoi(e) : 0;
-    return (t == 64 || t == 128 || t == 192) ? t : 0;
+    return (t == 128 || t == 256) ? t : 0;
   }();
   return v;
 }
 
-int gemm_common(const void* A, const uint8_t* tiles, const void* scales, void* C, bool fp32_out,
-                int M, int N, int K, int group, int variant, void* stream) {
-  if (!A || !tiles || !scales || !C) return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
+int check_shape(int M, int N, int K) {
   if (M < 1 || N < 128 || K < 64 || N % 128 != 0 || K % 64 != 0)
     return fail(I4G_ERR_SHAPE,
                 "shape M=%d N=%d K=%d: need M >= 1, N %% 128 == 0, K %% 64 == 0", M, N, K);
   if (static_cast<long long>(M) * K >= (1ll << 40) || static_cast<long long>(M) * N >= (1ll << 40))
     return fail(I4G_ERR_SHAPE, "shape M=%d N=%d K=%d too large", M, N, K);
-  int st = check_group(K, group, true);
+  return I4G_OK;
+}
+
+int tc_tile_m(int M, int N, const DeviceInfo* dev) {
+  return tile_m_override() ? tile_m_override() : i4g::tc::choose_tile_m(M, N, dev->sm_count);
+}
+
+// `workspace` (nullable) enables the split-K schedule of the tcgen05 kernel
+// when it holds at least the plan's bytes; otherwise the launch is unsplit.
+int gemm_common(const void* A, const uint8_t* tiles, const void* scales, void* C, bool fp32_out,
+                int M, int N, int K, int group, int variant, void* workspace,
+                size_t workspace_bytes, void* stream) {
+  if (!A || !tiles || !scales || !C) return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
+  int st = check_shape(M, N, K);
+  if (st != I4G_OK) return st;
+  st = check_group(K, group, true);
   if (st != I4G_OK) return st;
   if (!aligned(A, 16) || !aligned(tiles, 16) || !aligned(scales, 16) ||
       !aligned(C, fp32_out ? 4 : 2))
     return fail(I4G_ERR_ALIGNMENT, "A, tiles and scales must be 16-byte aligned");
+  if (workspace && !aligned(workspace, 256))
+    return fail(I4G_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
   if (variant != I4G_VARIANT_AUTO && variant != I4G_VARIANT_TC && variant != I4G_VARIANT_DECODE)
     return fail(I4G_ERR_VARIANT, "unknown variant %d", variant);
   if (variant == I4G_VARIANT_AUTO)
@@ -237,13 +252,16 @@ int gemm_common(const void* A, const uint8_t* tiles, const void* scales, void* C
                                    dev->sm_count, dev->status_word, g_wait_limit_ns, s),
                   "decode kernel launch");
   }
-  const int tile_m = tile_m_override() ? tile_m_override()
-                                       : i4g::tc::choose_tile_m(M, N, dev->sm_count);
+  const int tile_m = tc_tile_m(M, N, dev);
+  i4g::tc::Plan plan = i4g::tc::make_plan(tile_m, M, N, K, dev->sm_count, workspace != nullptr);
+  if (plan.workspace_bytes > workspace_bytes)
+    plan = i4g::tc::make_plan(tile_m, M, N, K, dev->sm_count, false);
   const CUtensorMap* map = nullptr;
   st = act_map(A, M, K, tile_m, &map);
   if (st != I4G_OK) return st;
   return finish(i4g::tc::launch(*map, tile_m, tiles, sc, C, fp32_out, M, N, K, group,
-                                dev->sm_count, dev->status_word, g_wait_limit_ns, s),
+                                dev->sm_count, plan, plan.split > 1 ? workspace : nullptr,
+                                dev->status_word, g_wait_limit_ns, s),
                 "tcgen05 kernel launch");
 }
 
@@ -423,17 +441,45 @@ int i4g_inverse_repack_umma(const uint8_t* tiles, uint8_t* packed, int K, int N,
 
 int i4g_gemm(const void* A, const uint8_t* tiles, const void* scales, void* C, int M, int N,
              int K, int group, void* stream) {
-  return gemm_common(A, tiles, scales, C, false, M, N, K, group, I4G_VARIANT_AUTO, stream);
+  return gemm_common(A, tiles, scales, C, false, M, N, K, group, I4G_VARIANT_AUTO, nullptr, 0,
+                     stream);
 }
 
 int i4g_gemm_fp32(const void* A, const uint8_t* tiles, const void* scales, float* C, int M,
                   int N, int K, int group, void* stream) {
-  return gemm_common(A, tiles, scales, C, true, M, N, K, group, I4G_VARIANT_TC, stream);
+  return gemm_common(A, tiles, scales, C, true, M, N, K, group, I4G_VARIANT_TC, nullptr, 0,
+                     stream);
 }
 
 int i4g_gemm_variant(const void* A, const uint8_t* tiles, const void* scales, void* C, int M,
                      int N, int K, int group, int variant, void* stream) {
-  return gemm_common(A, tiles, scales, C, false, M, N, K, group, variant, stream);
+  return gemm_common(A, tiles, scales, C, false, M, N, K, group, variant, nullptr, 0, stream);
+}
+
+int i4g_gemm_workspace_size(int M, int N, int K, size_t* bytes) {
+  if (!bytes) return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
+  *bytes = 0;
+  int st = check_shape(M, N, K);
+  if (st != I4G_OK) return st;
+  DeviceInfo* dev = nullptr;
+  if ((st = current_device(&dev)) != I4G_OK) return st;
+  if (M <= i4g::dec::MAX_M) return I4G_OK;  // the decode kernel needs none
+  *bytes = i4g::tc::make_plan(tc_tile_m(M, N, dev), M, N, K, dev->sm_count, true)
+               .workspace_bytes;
+  return I4G_OK;
+}
+
+int i4g_gemm_ws(const void* A, const uint8_t* tiles, const void* scales, void* C, int M, int N,
+                int K, int group, void* workspace, size_t workspace_bytes, void* stream) {
+  return gemm_common(A, tiles, scales, C, false, M, N, K, group, I4G_VARIANT_AUTO, workspace,
+                     workspace_bytes, stream);
+}
+
+int i4g_gemm_fp32_ws(const void* A, const uint8_t* tiles, const void* scales, float* C, int M,
+                     int N, int K, int group, void* workspace, size_t workspace_bytes,
+                     void* stream) {
+  return gemm_common(A, tiles, scales, C, true, M, N, K, group, I4G_VARIANT_TC, workspace,
+                     workspace_bytes, stream);
 }
 
 int i4g_shard_range(int K, int N, int group, int world, int rank, size_t* tile_offset,

@@ -32,6 +32,13 @@
 //   dfull/dempty[ACC]       accumulators in TMEM
 // The weight ring does not wait for the tensor core, so the dequant runs
 // ahead of the MMA by up to T_STAGES blocks.
+//
+// Schedule: work items are whole tiles, then (when the caller provides a
+// workspace) the tiles of the last, partial wave split along K into `split`
+// items each, so the last wave keeps every SM busy. A split item writes its
+// FP32 partial tile to the workspace and takes a ticket; the item that draws
+// the last ticket sums the partials in split order (deterministic) and writes
+// C, then resets the ticket counter for the next launch.
 #include "ptx.cuh"
 #include "gemm_tc.h"
 
@@ -88,6 +95,96 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
   nt = within / band_m;
 }
 
+struct Item {
+  int mt, nt, kb0, kb1;
+  int rem;  // index among the split tiles, or -1 for a whole tile
+  int f;    // K split index
+};
+
+__device__ __forceinline__ Item item_info(int item, int full_tiles, int split, int kblocks,
+                                          int num_m, int num_n) {
+  Item r;
+  int tile;
+  if (item < full_tiles) {
+    tile = item;
+    r.kb0 = 0;
+    r.kb1 = kblocks;
+    r.rem = -1;
+    r.f = 0;
+  } else {
+    const int j = item - full_tiles;
+    r.rem = j / split;
+    r.f = j - r.rem * split;
+    tile = full_tiles + r.rem;
+    r.kb0 = (r.f * kblocks) / split;
+    r.kb1 = ((r.f + 1) * kblocks) / split;
+  }
+  tile_coords(tile, num_m, num_n, r.mt, r.nt);
+  return r;
+}
+
+// Sums SPLIT partial tiles in split order (a fixed order, so results do not
+// depend on which CTA finished last) and writes quads*4 rows of column n of C,
+// starting at row m0. `base` points at this thread's first quad of split 0;
+// quads of one split are TILE_N float4 apart, splits (TILE_M/4)*TILE_N.
+// B quads are loaded for every split before any is summed, to overlap the
+// L2 latency.
+template <int TILE_M, int SPLIT, int B, bool FP32_OUT>
+__device__ __forceinline__ void reduce_partials(const float4* base, void* c_out, int m0, int n,
+                                                int M, int N, int quads) {
+  constexpr size_t kSplitStride = static_cast<size_t>(TILE_M / 4) * TILE_N;
+#pragma unroll 1
+  for (int q = 0; q < quads; q += B) {
+    float4 t[SPLIT][B];
+#pragma unroll
+    for (int f = 0; f < SPLIT; ++f)
+#pragma unroll
+      for (int b = 0; b < B; ++b)
+        t[f][b] = __ldcg(base + f * kSplitStride + static_cast<size_t>(q + b) * TILE_N);
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      float4 s = t[0][b];
+#pragma unroll
+      for (int f = 1; f < SPLIT; ++f) {
+        s.x += t[f][b].x;
+        s.y += t[f][b].y;
+        s.z += t[f][b].z;
+        s.w += t[f][b].w;
+      }
+      const float vals[4] = {s.x, s.y, s.z, s.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int m = m0 + 4 * (q + b) + i;
+        if (m < M) {
+          if constexpr (FP32_OUT)
+            static_cast<float*>(c_out)[static_cast<size_t>(m) * N + n] = vals[i];
+          else
+            static_cast<__half*>(c_out)[static_cast<size_t>(m) * N + n] = __float2half_rn(vals[i]);
+        }
+      }
+    }
+  }
+}
+
+// Named barrier among the epilogue warps (barrier 1); `bar_and` also ANDs a
+// per-thread predicate across them.
+__device__ __forceinline__ void epi_bar_sync(int nthreads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
+
+__device__ __forceinline__ bool epi_bar_and(int nthreads, bool v) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred pin, pout;\n\t"
+      "setp.ne.u32 pin, %1, 0;\n\t"
+      "bar.red.and.pred pout, 1, %2, pin;\n\t"
+      "selp.u32 %0, 1, 0, pout;\n\t}"
+      : "=r"(out)
+      : "r"(static_cast<uint32_t>(v)), "r"(nthreads)
+      : "memory");
+  return out != 0;
+}
+
 // Convert 32 fp32 accumulator columns of one lane into 16 packed halves.
 __device__ __forceinline__ void pack_half2(const uint32_t* v, uint32_t* out, int n) {
 #pragma unroll
@@ -121,8 +218,9 @@ template <int TILE_M, int GROUP, bool FP32_OUT>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap act_map,
                    const uint8_t* __restrict__ tiles, const __half* __restrict__ scales,
-                   void* __restrict__ c_out, int M, int N, int K, int* status,
-                   unsigned long long wait_limit_ns) {
+                   void* __restrict__ c_out, int M, int N, int K, int full_tiles, int split,
+                   int items, uint32_t* __restrict__ tickets, float* __restrict__ partials,
+                   int* status, unsigned long long wait_limit_ns) {
   using L = Cfg<TILE_M>;
   constexpr int A_STAGES = L::A_STAGES;
   constexpr int ACC = L::ACC;
@@ -151,12 +249,12 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t drain_bar = bar_base + 8u * (L::NUM_BARS - 1);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC_OFF + 4);
+  volatile uint32_t* ticket_slot = reinterpret_cast<volatile uint32_t*>(smem + L::MISC_OFF + 8);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_m = (M + TILE_M - 1) / TILE_M;
   const int num_n = N / TILE_N;
-  const int num_tiles = num_m * num_n;
   const int kblocks = K / BK;
   const int groups = K / GROUP;
 
@@ -199,10 +297,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       int last_issue[A_STAGES];
       for (int s = 0; s < A_STAGES; ++s) last_issue[s] = -1;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        int mt, nt;
-        tile_coords(tile, num_m, num_n, mt, nt);
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+      for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
+        const Item w = item_info(item, full_tiles, split, kblocks, num_m, num_n);
+        const int mt = w.mt;
+        for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
           const int s = it % A_STAGES;
           const uint32_t ph = (it / A_STAGES) & 1u;
           if (!mbar_wait(aempty(s), ph ^ 1u, abort_flag, status, wait_limit_ns)) {
@@ -229,12 +327,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       int last_issue[W_STAGES];
       for (int s = 0; s < W_STAGES; ++s) last_issue[s] = -1;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        int mt, nt;
-        tile_coords(tile, num_m, num_n, mt, nt);
-        const uint8_t* wblk = tiles + static_cast<size_t>(nt) * kblocks * WBLOCK_BYTES;
-        const __half* sblk = scales + static_cast<size_t>(nt) * groups * TILE_N;
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+      for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
+        const Item w = item_info(item, full_tiles, split, kblocks, num_m, num_n);
+        const uint8_t* wblk = tiles + static_cast<size_t>(w.nt) * kblocks * WBLOCK_BYTES;
+        const __half* sblk = scales + static_cast<size_t>(w.nt) * groups * TILE_N;
+        for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
           const int s = it % W_STAGES;
           const uint32_t ph = (it / W_STAGES) & 1u;
           if (!mbar_wait(wempty(s), ph ^ 1u, abort_flag, status, wait_limit_ns)) {
@@ -267,7 +364,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       constexpr uint32_t IDESC = idesc_f16_f32(TILE_N, TILE_M);
       uint32_t it = 0, t_local = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++t_local) {
+      for (int item = blockIdx.x; item < items && ok; item += gridDim.x, ++t_local) {
+        const Item w = item_info(item, full_tiles, split, kblocks, num_m, num_n);
         const int acc = t_local % ACC;
         const uint32_t dph = (t_local / ACC) & 1u;
         if (!mbar_wait(dempty(acc), dph ^ 1u, abort_flag, status, wait_limit_ns)) {
@@ -276,7 +374,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + ACC_COL0 + acc * TILE_M;
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
           const int s = it % A_STAGES;
           const uint32_t ph = (it / A_STAGES) & 1u;
           const int ts = it % T_STAGES;
@@ -292,7 +390,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int k16 = 0; k16 < BK / 16; ++k16) {
             const uint32_t a_tmem = tmem_base + ts * T_COLS + k16 * 8;
             const uint64_t b_desc = smem_desc_sw128(b_addr + k16 * 32);
-            mma_f16_ts(d_tmem, a_tmem, b_desc, IDESC, (kb | k16) != 0);
+            mma_f16_ts(d_tmem, a_tmem, b_desc, IDESC, (kb != w.kb0) || (k16 != 0));
           }
           tc_commit(aempty(s));
           tc_commit(tempty(ts));
@@ -312,10 +410,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int row = quarter * 32 + lane;   // weight column inside the tile
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     uint32_t it = static_cast<uint32_t>(dgroup);
-    const uint32_t total = static_cast<uint32_t>(kblocks) *
-                           static_cast<uint32_t>((num_tiles - static_cast<int>(blockIdx.x) +
-                                                  static_cast<int>(gridDim.x) - 1) /
-                                                 static_cast<int>(gridDim.x));
+    uint32_t total = 0;  // 64-k blocks this CTA processes, over all its items
+    for (int item = blockIdx.x; item < items; item += gridDim.x) {
+      const Item w = item_info(item, full_tiles, split, kblocks, num_m, num_n);
+      total += static_cast<uint32_t>(w.kb1 - w.kb0);
+    }
     for (; it < total; it += DEQ_GROUPS) {
       const int s = it % W_STAGES;
       const uint32_t ph = (it / W_STAGES) & 1u;
@@ -369,63 +468,124 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int half = e >> 2;  // which quarter of the columns
     const int row = quarter * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    constexpr int EPI_THREADS = NUM_EPI_WARPS * 32;
     uint32_t t_local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t_local) {
-      int mt, nt;
-      tile_coords(tile, num_m, num_n, mt, nt);
+    bool failed = false;
+    for (int item = blockIdx.x; item < items; item += gridDim.x, ++t_local) {
+      const Item w = item_info(item, full_tiles, split, kblocks, num_m, num_n);
       const int acc = t_local % ACC;
       const uint32_t dph = (t_local / ACC) & 1u;
-      if (!mbar_wait(dfull(acc), dph, abort_flag, status, wait_limit_ns)) break;
-      tc_fence_after();
+      const bool ok = !failed && mbar_wait(dfull(acc), dph, abort_flag, status, wait_limit_ns);
       const uint32_t col0 = tmem_base + lane_addr + ACC_COL0 + acc * TILE_M + half * COLS;
-      const int n = nt * TILE_N + row;
-      const int m0 = mt * TILE_M + half * COLS;
-      if constexpr (FP32_OUT) {
-        // FP32 C: store each 16-column chunk as it is read.
-        float* cp = static_cast<float*>(c_out) + static_cast<size_t>(m0) * N + n;
+      const int n = w.nt * TILE_N + row;
+      const int m0 = w.mt * TILE_M + half * COLS;
+      if (w.rem < 0) {
+        // ------------------------------------------------ whole tile -> C
+        if (!ok) {
+          failed = true;
+          continue;
+        }
+        tc_fence_after();
+        if constexpr (FP32_OUT) {
+          // FP32 C: store each 16-column chunk as it is read.
+          float* cp = static_cast<float*>(c_out) + static_cast<size_t>(m0) * N + n;
+#pragma unroll 1
+          for (int c = 0; c < COLS / 16; ++c) {
+            uint32_t v[16];
+            tmem_ld_32x32b_x16(col0 + c * 16, v);
+            tmem_ld_wait16(v);
+            if (c == COLS / 16 - 1) {
+              tc_fence_before();
+              mbar_arrive(dempty(acc));
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (m0 + c * 16 + j < M)
+                cp[static_cast<size_t>(c * 16 + j) * N] = __uint_as_float(v[j]);
+          }
+        } else {
+          uint32_t h[COLS / 2];  // packed halves: h[j] = columns 2j, 2j+1
+#pragma unroll
+          for (int c = 0; c < COLS / 16; ++c) {
+            uint32_t v[16];
+            tmem_ld_32x32b_x16(col0 + c * 16, v);
+            tmem_ld_wait16(v);
+            pack_half2(v, &h[c * 8], 8);
+          }
+          tc_fence_before();
+          mbar_arrive(dempty(acc));
+          __half* cp = static_cast<__half*>(c_out) + static_cast<size_t>(m0) * N + n;
+          const int valid = min(COLS, M - m0);
+          if (valid >= COLS) {
+#pragma unroll
+            for (int j = 0; j < COLS / 2; ++j) {
+              const __half2 hv = *reinterpret_cast<const __half2*>(&h[j]);
+              cp[static_cast<size_t>(2 * j) * N] = __low2half(hv);
+              cp[static_cast<size_t>(2 * j + 1) * N] = __high2half(hv);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < COLS / 2; ++j) {
+              const __half2 hv = *reinterpret_cast<const __half2*>(&h[j]);
+              if (2 * j < valid) cp[static_cast<size_t>(2 * j) * N] = __low2half(hv);
+              if (2 * j + 1 < valid) cp[static_cast<size_t>(2 * j + 1) * N] = __high2half(hv);
+            }
+          }
+        }
+        continue;
+      }
+      // ------------------------------------------------ split item -> partial
+      // Every epilogue warp takes the same barriers below whatever happened,
+      // so a failed wait cannot strand the others at a barrier. A partial
+      // tile is stored as float4 quads [m / 4][n][m % 4], so that each warp
+      // access is 512 contiguous bytes.
+      float4* mine = reinterpret_cast<float4*>(partials) +
+                     static_cast<size_t>(w.rem * split + w.f) * (TILE_M / 4) * TILE_N;
+      if (ok) {
+        tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < COLS / 16; ++c) {
           uint32_t v[16];
           tmem_ld_32x32b_x16(col0 + c * 16, v);
           tmem_ld_wait16(v);
-          if (c == COLS / 16 - 1) {
-            tc_fence_before();
-            mbar_arrive(dempty(acc));
-          }
+          const int q0 = (half * COLS + c * 16) / 4;
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            if (m0 + c * 16 + j < M)
-              cp[static_cast<size_t>(c * 16 + j) * N] = __uint_as_float(v[j]);
-        }
-      } else {
-        uint32_t h[COLS / 2];  // packed halves: h[j] = columns 2j, 2j+1
-#pragma unroll
-        for (int c = 0; c < COLS / 16; ++c) {
-          uint32_t v[16];
-          tmem_ld_32x32b_x16(col0 + c * 16, v);
-          tmem_ld_wait16(v);
-          pack_half2(v, &h[c * 8], 8);
+          for (int j = 0; j < 4; ++j)
+            __stcg(mine + static_cast<size_t>(q0 + j) * TILE_N + row,
+                   make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                               __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3])));
         }
         tc_fence_before();
         mbar_arrive(dempty(acc));
-        __half* cp = static_cast<__half*>(c_out) + static_cast<size_t>(m0) * N + n;
-        const int valid = min(COLS, M - m0);
-        if (valid >= COLS) {
-#pragma unroll
-          for (int j = 0; j < COLS / 2; ++j) {
-            const __half2 hv = *reinterpret_cast<const __half2*>(&h[j]);
-            cp[static_cast<size_t>(2 * j) * N] = __low2half(hv);
-            cp[static_cast<size_t>(2 * j + 1) * N] = __high2half(hv);
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < COLS / 2; ++j) {
-            const __half2 hv = *reinterpret_cast<const __half2*>(&h[j]);
-            if (2 * j < valid) cp[static_cast<size_t>(2 * j) * N] = __low2half(hv);
-            if (2 * j + 1 < valid) cp[static_cast<size_t>(2 * j + 1) * N] = __high2half(hv);
-          }
+        __threadfence();
+      }
+      if (!epi_bar_and(EPI_THREADS, ok)) {
+        failed = true;
+        continue;
+      }
+      if (warp == FIRST_EPI_WARP && lane == 0) *ticket_slot = atomicAdd(&tickets[w.rem], 1u);
+      epi_bar_sync(EPI_THREADS);
+      const bool last = *ticket_slot == static_cast<uint32_t>(split - 1);
+      if (last) {
+        __threadfence();
+        const float4* base = reinterpret_cast<const float4*>(partials) +
+                             static_cast<size_t>(w.rem * split) * (TILE_M / 4) * TILE_N +
+                             static_cast<size_t>(half * COLS / 4) * TILE_N + row;
+        const int mq = w.mt * TILE_M + half * COLS;
+        switch (split) {
+          case 2:
+            reduce_partials<TILE_M, 2, 4, FP32_OUT>(base, c_out, mq, n, M, N, COLS / 4);
+            break;
+          case 3:
+            reduce_partials<TILE_M, 3, 2, FP32_OUT>(base, c_out, mq, n, M, N, COLS / 4);
+            break;
+          default:
+            reduce_partials<TILE_M, 4, 2, FP32_OUT>(base, c_out, mq, n, M, N, COLS / 4);
+            break;
         }
       }
+      epi_bar_sync(EPI_THREADS);  // the ticket slot is read by all before it changes
+      if (last && warp == FIRST_EPI_WARP && lane == 0) tickets[w.rem] = 0u;
     }
   }
 
@@ -440,10 +600,34 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 // ------------------------------------------------------------------- host
 
+Plan make_plan(int tile_m, int M, int N, int K, int sm_count, bool allow_split) {
+  Plan p;
+  const int tiles = ((M + tile_m - 1) / tile_m) * (N / TILE_N);
+  p.full_tiles = tiles;
+  p.split = 1;
+  p.items = tiles;
+  p.workspace_bytes = 0;
+  if (!allow_split) return p;
+  const int waves = tiles / sm_count;
+  const int rem = tiles - waves * sm_count;
+  if (rem == 0 || rem * 4 > static_cast<int>(kTicketBytes)) return p;
+  int f = sm_count / rem;
+  f = f < 4 ? f : 4;
+  const int kcap = (K / BK) / 8;  // each split keeps at least eight 64-k blocks
+  f = f < kcap ? f : kcap;
+  if (f < 2) return p;
+  p.full_tiles = waves * sm_count;
+  p.split = f;
+  p.items = p.full_tiles + rem * f;
+  p.workspace_bytes = kTicketBytes + static_cast<size_t>(rem) * f * tile_m * TILE_N * 4;
+  return p;
+}
+
 template <int TILE_M, int GROUP, bool FP32_OUT>
 cudaError_t launch_impl(const CUtensorMap& act_map, const uint8_t* tiles, const __half* scales,
-                        void* c, int M, int N, int K, int sm_count, int* status,
-                        unsigned long long wait_limit_ns, cudaStream_t stream) {
+                        void* c, int M, int N, int K, int sm_count, const Plan& plan,
+                        void* workspace, int* status, unsigned long long wait_limit_ns,
+                        cudaStream_t stream) {
   using L = Cfg<TILE_M>;
   auto kernel = gemm_tc_kernel<TILE_M, GROUP, FP32_OUT>;
   static bool configured = false;  // per instantiation; idempotent attribute
@@ -453,28 +637,32 @@ cudaError_t launch_impl(const CUtensorMap& act_map, const uint8_t* tiles, const 
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  const int num_tiles = ((M + TILE_M - 1) / TILE_M) * (N / TILE_N);
-  const int grid = num_tiles < sm_count ? num_tiles : sm_count;
-  kernel<<<grid, THREADS, L::DYN_BYTES, stream>>>(act_map, tiles, scales, c, M, N, K, status,
-                                                  wait_limit_ns);
+  const int grid = plan.items < sm_count ? plan.items : sm_count;
+  uint32_t* tickets = static_cast<uint32_t*>(workspace);
+  float* partials = workspace ? reinterpret_cast<float*>(static_cast<char*>(workspace) +
+                                                         kTicketBytes)
+                              : nullptr;
+  kernel<<<grid, THREADS, L::DYN_BYTES, stream>>>(act_map, tiles, scales, c, M, N, K,
+                                                  plan.full_tiles, plan.split, plan.items,
+                                                  tickets, partials, status, wait_limit_ns);
   return cudaGetLastError();
 }
 
 template <int TILE_M, bool FP32_OUT>
 cudaError_t launch_group(const CUtensorMap& act_map, const uint8_t* tiles,
                          const __half* scales, void* c, int M, int N, int K, int group,
-                         int sm_count, int* status, unsigned long long wait_limit_ns,
-                         cudaStream_t stream) {
+                         int sm_count, const Plan& plan, void* workspace, int* status,
+                         unsigned long long wait_limit_ns, cudaStream_t stream) {
   switch (group) {
     case 32:
       return launch_impl<TILE_M, 32, FP32_OUT>(act_map, tiles, scales, c, M, N, K, sm_count,
-                                               status, wait_limit_ns, stream);
+                                               plan, workspace, status, wait_limit_ns, stream);
     case 64:
       return launch_impl<TILE_M, 64, FP32_OUT>(act_map, tiles, scales, c, M, N, K, sm_count,
-                                               status, wait_limit_ns, stream);
+                                               plan, workspace, status, wait_limit_ns, stream);
     default:
       return launch_impl<TILE_M, 128, FP32_OUT>(act_map, tiles, scales, c, M, N, K, sm_count,
-                                                status, wait_limit_ns, stream);
+                                                plan, workspace, status, wait_limit_ns, stream);
   }
 }
 
@@ -488,14 +676,16 @@ int choose_tile_m(int M, int N, int sm_count) {
 
 cudaError_t launch(const CUtensorMap& act_map, int tile_m, const uint8_t* tiles,
                    const __half* scales, void* c, bool fp32_out, int M, int N, int K, int group,
-                   int sm_count, int* status, unsigned long long wait_limit_ns,
-                   cudaStream_t stream) {
+                   int sm_count, const Plan& plan, void* workspace, int* status,
+                   unsigned long long wait_limit_ns, cudaStream_t stream) {
 #define I4G_TC_CASE(TM)                                                                       \
   if (tile_m == TM)                                                                           \
     return fp32_out ? launch_group<TM, true>(act_map, tiles, scales, c, M, N, K, group,       \
-                                             sm_count, status, wait_limit_ns, stream)         \
+                                             sm_count, plan, workspace, status,               \
+                                             wait_limit_ns, stream)                           \
                     : launch_group<TM, false>(act_map, tiles, scales, c, M, N, K, group,      \
-                                              sm_count, status, wait_limit_ns, stream);
+                                              sm_count, plan, workspace, status,              \
+                                              wait_limit_ns, stream);
   I4G_TC_CASE(128)
   I4G_TC_CASE(256)
 #undef I4G_TC_CASE

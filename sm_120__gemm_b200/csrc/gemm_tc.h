@@ -8,12 +8,23 @@
 
 namespace i4g {
 namespace tc {
+// Ticket counters at the start of a split-K workspace, then the FP32 partials.
+constexpr size_t kTicketBytes = 1024;
+
+// Work schedule of one launch: `full_tiles` whole tiles, then the remaining
+// tiles split `split` ways along K (items = full_tiles + rest * split).
+struct Plan {
+  int full_tiles, split, items;
+  size_t workspace_bytes;  // 0 when nothing is split
+};
+Plan make_plan(int tile_m, int M, int N, int K, int sm_count, bool allow_split);
+
 // TILE_M (activation rows per tile, the MMA-N) for a problem on sm_count SMs.
 int choose_tile_m(int M, int N, int sm_count);
 cudaError_t launch(const CUtensorMap& act_map, int tile_m, const uint8_t* tiles,
                    const __half* scales, void* c, bool fp32_out, int M, int N, int K,
-                   int group, int sm_count, int* status, unsigned long long wait_limit_ns,
-                   cudaStream_t stream);
+                   int group, int sm_count, const Plan& plan, void* workspace, int* status,
+                   unsigned long long wait_limit_ns, cudaStream_t stream);
 }  // namespace tc
 
 namespace dec {

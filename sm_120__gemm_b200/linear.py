@@ -9,8 +9,8 @@ from __future__ import annotations
 
 import torch
 
-from . import (launch_final, launch_final_fp32, launch_quantize, launch_repack_scales_128,
-               launch_repack_umma, shard_range)
+from . import (launch_final_fp32_ws, launch_final_ws, launch_quantize,
+               launch_repack_scales_128, launch_repack_umma, shard_range, workspace_for)
 
 
 class QuantizedLinear:
@@ -65,6 +65,7 @@ class QuantizedLinear:
         if out is None:
             out = torch.empty(M, self.N, dtype=torch.float32 if fp32_out else torch.float16,
                               device=a.device)
-        fn = launch_final_fp32 if fp32_out else launch_final
-        fn(a, self.tiles, self.scales, out, M, self.N, self.K, self.group, stream)
+        ws = workspace_for(M, self.N, self.K, a.device, stream)
+        fn = launch_final_fp32_ws if fp32_out else launch_final_ws
+        fn(a, self.tiles, self.scales, out, M, self.N, self.K, self.group, ws, stream)
         return out

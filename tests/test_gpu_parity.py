@@ -214,7 +214,9 @@ def test_gemm_deterministic(i4g):
     lin = i4g.QuantizedLinear.from_weight(w.cuda(), 64)
     ad = a.cuda()
     for _ in range(5):
-        outs.append(lin(ad).clone())
+        c = torch.empty(M, N, dtype=torch.float16, device="cuda")
+        i4g.launch_final(ad, lin.tiles, lin.scales, c, M, N, K, 64)
+        outs.append(c)
     torch.cuda.synchronize()
     for o in outs[1:]:
         assert torch.equal(o.view(torch.int16), outs[0].view(torch.int16))

@@ -1,0 +1,152 @@
+"""Split-K schedule of the tcgen05 kernel (the *_ws entry points).
+
+The tiles of the last, partial wave are split along K and reduced through a
+caller-owned FP32 workspace in a fixed order. Results are checked against the
+oracle under the same tolerance as the unsplit kernel (tests/parity.py), are
+bitwise reproducible, and leave the workspace counters at zero.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from parity import fp32_report, gemm_report, make_inputs, u16
+
+pytestmark = pytest.mark.gpu
+
+TICKET_BYTES = 1024
+TILE_N = 128
+
+
+@pytest.fixture(scope="module")
+def i4g():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    import sm_120__gemm_b200 as m
+    m.load()
+    return m
+
+
+def expected_plan(M, N, K):
+    """(split, remainder tiles) the host plans for this shape on cuda:0."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    tile_m = 128 if M <= 128 else 256
+    tiles = -(-M // tile_m) * (N // TILE_N)
+    rem = tiles % sms
+    f = min(4, sms // rem if rem else 0, (K // 64) // 8)
+    if rem == 0 or f < 2:
+        return 1, 0, tile_m
+    return f, rem, tile_m
+
+
+def fresh_workspace(i4g, M, N, K):
+    n = i4g.gemm_workspace_size(M, N, K)
+    return torch.zeros(max(n, 256), dtype=torch.uint8, device="cuda"), n
+
+
+@pytest.mark.parametrize("M,N,K", [(4096, 4096, 4096), (512, 1024, 4096), (300, 640, 2048),
+                                   (16, 4096, 4096), (4096, 4096, 448), (2048, 9472, 1024)])
+def test_workspace_size(i4g, M, N, K):
+    f, rem, tile_m = expected_plan(M, N, K)
+    want = 0 if (f == 1 or M <= 16) else TICKET_BYTES + rem * f * tile_m * TILE_N * 4
+    assert i4g.gemm_workspace_size(M, N, K) == want
+
+
+def split_case(i4g, M, N, K, grp, rows=None, fp32_out=False, seed=0):
+    a, w = make_inputs(M, N, K, seed_a=99 + seed, seed_b=77 + seed)
+    a16, w16 = u16(a), u16(w)
+    packed_np, scales_np = oracle.quantize(w16, K, N, grp)
+    lin = i4g.QuantizedLinear.from_weight(w.cuda(), grp)
+    ws, need = fresh_workspace(i4g, M, N, K)
+    dt = torch.float32 if fp32_out else torch.float16
+    c = torch.empty(M, N, dtype=dt, device="cuda")
+    fn = i4g.launch_final_fp32_ws if fp32_out else i4g.launch_final_ws
+    fn(a.cuda(), lin.tiles, lin.scales, c, M, N, K, grp, ws)
+    torch.cuda.synchronize()
+    assert i4g.device_status() == 0
+    assert int(ws[:TICKET_BYTES].count_nonzero()) == 0, "arrival counters not reset"
+    deq = oracle.dequantize(packed_np, scales_np, K, N, grp)
+    rows = np.arange(M) if rows is None else np.asarray(rows)
+    ref32 = oracle.gemm_rows(a16, deq, M, N, K, rows=rows, threads=8)
+    abs32 = oracle.abs_gemm_rows(a16, deq, M, N, K, rows=rows)
+    if fp32_out:
+        rep = fp32_report(c.cpu().numpy()[rows], ref32, abs32, K)
+    else:
+        rep = gemm_report(u16(c)[rows], ref32, abs32, K)
+    return rep, c, (a.cuda(), lin, ws)
+
+
+@pytest.mark.parametrize("M,N,K,grp", [(512, 1024, 4096, 128), (300, 640, 2048, 32),
+                                       (1000, 1280, 1024, 64), (130, 384, 1536, 64),
+                                       (2048, 9600, 1024, 32)])
+def test_split_parity(i4g, M, N, K, grp):
+    assert expected_plan(M, N, K)[0] > 1, "shape chosen to exercise the split"
+    rep, _, _ = split_case(i4g, M, N, K, grp)
+    print("split", M, N, K, grp, rep)
+    assert rep["ok"], rep
+
+
+@pytest.mark.parametrize("grp", [32, 128])
+def test_split_4096_sampled_rows(i4g, grp):
+    M = N = K = 4096
+    # rows in the first whole-tile waves and in the split last wave (the
+    # last tiles in schedule order are the highest row blocks of the last
+    # column groups)
+    rows = np.concatenate([np.arange(0, 8), np.arange(250, 262), np.arange(3830, 3842),
+                           np.arange(4088, 4096)])
+    rep, _, _ = split_case(i4g, M, N, K, grp, rows=rows)
+    print("split 4096^3 g", grp, rep)
+    assert rep["ok"], rep
+
+
+@pytest.mark.parametrize("M,N,K,grp", [(512, 1024, 4096, 64), (300, 640, 2048, 128)])
+def test_split_fp32_output(i4g, M, N, K, grp):
+    rep, _, _ = split_case(i4g, M, N, K, grp, fp32_out=True)
+    print("split fp32", M, N, K, grp, rep)
+    assert rep["ok"], rep
+
+
+def test_split_reuse_is_bitwise_reproducible(i4g):
+    """One workspace across launches of different shapes: every launch
+    returns the counters to zero, so repeated results are bitwise equal."""
+    _, c_a, (a_a, lin_a, _) = split_case(i4g, 512, 1024, 4096, 128, rows=np.arange(2))
+    _, c_b, (a_b, lin_b, _) = split_case(i4g, 1000, 1280, 1024, 64, rows=np.arange(2), seed=1)
+    need = max(i4g.gemm_workspace_size(512, 1024, 4096), i4g.gemm_workspace_size(1000, 1280, 1024))
+    ws = torch.zeros(need, dtype=torch.uint8, device="cuda")
+    for _ in range(3):
+        for (a, lin, ref, M) in ((a_a, lin_a, c_a, 512), (a_b, lin_b, c_b, 1000)):
+            c = torch.empty_like(ref)
+            i4g.launch_final_ws(a, lin.tiles, lin.scales, c, M, lin.N, lin.K, lin.group, ws)
+            torch.cuda.synchronize()
+            assert torch.equal(c.view(torch.int16), ref.view(torch.int16))
+    assert i4g.device_status() == 0
+    assert int(ws[:TICKET_BYTES].count_nonzero()) == 0
+
+
+def test_small_workspace_runs_unsplit(i4g):
+    """A workspace smaller than needed (or none) selects the unsplit schedule,
+    bitwise equal to i4g_gemm."""
+    M, N, K, grp = 512, 1024, 4096, 128
+    a, w = make_inputs(M, N, K)
+    lin = i4g.QuantizedLinear.from_weight(w.cuda(), grp)
+    ad = a.cuda()
+    c0 = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    i4g.launch_final(ad, lin.tiles, lin.scales, c0, M, N, K, grp)
+    small = torch.zeros(1024, dtype=torch.uint8, device="cuda")
+    for ws in (None, small):
+        c = torch.empty_like(c0)
+        i4g.launch_final_ws(ad, lin.tiles, lin.scales, c, M, N, K, grp, ws)
+        torch.cuda.synchronize()
+        assert torch.equal(c.view(torch.int16), c0.view(torch.int16))
+
+
+def test_misaligned_workspace_rejected(i4g):
+    M, N, K = 512, 1024, 4096
+    ws = torch.zeros(i4g.gemm_workspace_size(M, N, K) + 512, dtype=torch.uint8, device="cuda")
+    a = torch.zeros(M, K, dtype=torch.float16, device="cuda")
+    tiles = torch.zeros(K * N // 2, dtype=torch.uint8, device="cuda")
+    scales = torch.zeros(K // 128 * N, dtype=torch.float16, device="cuda")
+    c = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    with pytest.raises(i4g.I4GError) as e:
+        i4g.launch_final_ws(a, tiles, scales, c, M, N, K, 128, ws[16:])
+    assert e.value.status == -4
