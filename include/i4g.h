@@ -157,6 +157,24 @@ int i4g_gemm_fp32_ws(const void* A, const uint8_t* tiles, const void* scales,
                      float* C, int M, int N, int K, int group, void* workspace,
                      size_t workspace_bytes, void* stream);
 
+/* ---- GEMM without any allocation (no counterpart in the reference) -------- */
+
+/* i4g_gemm_ws for callers that cannot allocate device memory or own a
+ * workspace (e.g. a host framework whose memory is fully pooled, or a plugin
+ * given only A, B and C): the split-K workspace is a fixed 20 MiB array in
+ * static device memory, one per device, so nothing is allocated per call.
+ * Limit: shapes whose split-K workspace exceeds 20 MiB are rejected with
+ * I4G_ERR_SHAPE (none on a device with up to 159 SMs; B200 has 148).
+ * Set-up: the first call on a device loads the scratch and looks up its
+ * address with that device current; make that call before any stream
+ * capture. Each call clears the scratch's 1 KiB of arrival counters on
+ * `stream` before its launch (they must start at zero).
+ * Calls on one device share the scratch: calls that overlap in time (e.g. on
+ * two streams without ordering between them) race and give wrong results. */
+int i4g_gemm_static_scratch(const void* A, const uint8_t* tiles,
+                            const void* scales, void* C, int M, int N, int K,
+                            int group, void* stream);
+
 /* ---- column-parallel sharding --------------------------------------------- */
 
 /* Byte offsets of rank `rank`'s slice of a G-way column-parallel split of the

@@ -482,6 +482,39 @@ int i4g_gemm_fp32_ws(const void* A, const uint8_t* tiles, const void* scales, fl
                      workspace_bytes, stream);
 }
 
+int i4g_gemm_static_scratch(const void* A, const uint8_t* tiles, const void* scales, void* C,
+                            int M, int N, int K, int group, void* stream) {
+  int st = check_shape(M, N, K);
+  if (st != I4G_OK) return st;
+  DeviceInfo* dev = nullptr;
+  if ((st = current_device(&dev)) != I4G_OK) return st;
+  size_t need = 0;
+  if (M > i4g::dec::MAX_M)
+    need = i4g::tc::make_plan(tc_tile_m(M, N, dev), M, N, K, dev->sm_count, true)
+               .workspace_bytes;
+  if (need > i4g::static_scratch_bytes()) {
+    std::snprintf(t_last_error, sizeof(t_last_error),
+                  "shape M=%d N=%d K=%d needs %zu bytes of split-K scratch; the static scratch "
+                  "holds %zu",
+                  M, N, K, need, i4g::static_scratch_bytes());
+    return I4G_ERR_SHAPE;
+  }
+  void* scratch = nullptr;
+  if (need > 0) {
+    int ordinal = -1;
+    cudaError_t e = cudaGetDevice(&ordinal);
+    if (e == cudaSuccess) e = i4g::static_scratch(ordinal, &scratch);
+    if (e != cudaSuccess) return record_cuda(e, "cudaGetSymbolAddress(static scratch)");
+    // The arrival counters must be zero when the kernel starts. Completed
+    // launches leave them so; clearing them here keeps a launch that gave up
+    // on a device-side wait from corrupting the next call.
+    e = cudaMemsetAsync(scratch, 0, i4g::tc::kTicketBytes, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return record_cuda(e, "clearing the static scratch counters");
+  }
+  return gemm_common(A, tiles, scales, C, false, M, N, K, group, I4G_VARIANT_AUTO, scratch, need,
+                     stream);
+}
+
 int i4g_shard_range(int K, int N, int group, int world, int rank, size_t* tile_offset,
                     size_t* scale_offset, int* n0, int* n1) {
   if (!tile_offset || !scale_offset || !n0 || !n1)

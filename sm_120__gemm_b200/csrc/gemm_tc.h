@@ -56,4 +56,8 @@ cudaError_t repack_umma(const uint8_t* packed, uint8_t* tiles, int K, int N,
 cudaError_t inverse_repack_umma(const uint8_t* tiles, uint8_t* packed, int K, int N,
                                 cudaStream_t stream);
 }  // namespace prep
+
+// Fixed-size split-K scratch in static device memory (static_scratch.cu).
+size_t static_scratch_bytes();
+cudaError_t static_scratch(int device, void** out);
 }  // namespace i4g
