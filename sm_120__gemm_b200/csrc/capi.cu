@@ -124,9 +124,10 @@ int encode_fn(EncodeTiledFn* out) {
 }
 
 // Activation map of A [M][K] fp16, 128-byte swizzle, zero fill past M:
-// rows > 0 gives the 2-D box 64 (K) x rows (M); rows < 0 the 3-D box of
-// four consecutive 64-k blocks x -rows rows. A few recent maps are cached per host thread, keyed by
-// pointer and shape, as the reference caches its maps
+// rows > 0 gives the 2-D box 64 (K) x rows (M) of the tcgen05 kernel; rows < 0
+// the 3-D box of four consecutive 64-k blocks x -rows rows of the decode
+// kernel. A few recent maps are cached per host thread, keyed by pointer and
+// shape, as the reference caches its maps
 // (kernels/gemm_v17_instruction.cu:214-228).
 struct ActMapEntry {
   int device = -1;
@@ -157,7 +158,7 @@ int act_map(const void* A, int M, int K, int rows, const CUtensorMap** out) {
   if (st != I4G_OK) return st;
   CUresult r;
   if (rows > 0) {
-    // 2-D view [M][K]: box of 64 k x `rows` rows (the tcgen05 kernel)
+    // 2-D view [M][K]: box of 64 k x `rows` rows
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
     const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(rows)};
@@ -166,8 +167,7 @@ int act_map(const void* A, int M, int K, int rows, const CUtensorMap** out) {
                strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   } else {
-    // 3-D view {64 k, M rows, K/64 blocks}: box of 64 k x -rows rows x 4
-    // blocks (the decode kernel's ring stage)
+    // 3-D view {64 k, M rows, K/64 blocks}: box of 64 k x -rows rows x 4 blocks
     const cuuint64_t dims[3] = {64, static_cast<cuuint64_t>(M), static_cast<cuuint64_t>(K / 64)};
     const cuuint64_t strides[2] = {static_cast<cuuint64_t>(K) * 2, 128};
     const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(-rows), 4};
@@ -235,10 +235,13 @@ int gemm_common(const void* A, const uint8_t* tiles, const void* scales, void* C
   if (variant != I4G_VARIANT_AUTO && variant != I4G_VARIANT_TC && variant != I4G_VARIANT_DECODE)
     return fail(I4G_ERR_VARIANT, "unknown variant %d", variant);
   if (variant == I4G_VARIANT_AUTO)
-    variant = (!fp32_out && M <= i4g::dec::MAX_M) ? I4G_VARIANT_DECODE : I4G_VARIANT_TC;
+    variant = (!fp32_out && i4g::dec::supported(M, K, group)) ? I4G_VARIANT_DECODE
+                                                              : I4G_VARIANT_TC;
   if (variant == I4G_VARIANT_DECODE && (fp32_out || M > i4g::dec::MAX_M))
     return fail(I4G_ERR_VARIANT, "decode variant needs M <= %d and an FP16 C (M=%d)",
                 i4g::dec::MAX_M, M);
+  if (variant == I4G_VARIANT_DECODE && !i4g::dec::supported(M, K, group))
+    return fail(I4G_ERR_SHAPE, "decode variant: K=%d too large for its shared memory", K);
   DeviceInfo* dev = nullptr;
   st = current_device(&dev);
   if (st != I4G_OK) return st;
@@ -463,7 +466,8 @@ int i4g_gemm_workspace_size(int M, int N, int K, size_t* bytes) {
   if (st != I4G_OK) return st;
   DeviceInfo* dev = nullptr;
   if ((st = current_device(&dev)) != I4G_OK) return st;
-  if (M <= i4g::dec::MAX_M) return I4G_OK;  // the decode kernel needs none
+  // the decode kernel needs none (its largest-K limit is for group 32)
+  if (i4g::dec::supported(M, K, 32)) return I4G_OK;
   *bytes = i4g::tc::make_plan(tc_tile_m(M, N, dev), M, N, K, dev->sm_count, true)
                .workspace_bytes;
   return I4G_OK;
@@ -489,7 +493,7 @@ int i4g_gemm_static_scratch(const void* A, const uint8_t* tiles, const void* sca
   DeviceInfo* dev = nullptr;
   if ((st = current_device(&dev)) != I4G_OK) return st;
   size_t need = 0;
-  if (M > i4g::dec::MAX_M)
+  if (!i4g::dec::supported(M, K, group))
     need = i4g::tc::make_plan(tc_tile_m(M, N, dev), M, N, K, dev->sm_count, true)
                .workspace_bytes;
   if (need > i4g::static_scratch_bytes()) {

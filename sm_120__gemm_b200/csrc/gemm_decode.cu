@@ -14,39 +14,34 @@
 // set of products, accumulated in FP32.
 //
 // Work split: a CTA owns one 128-column tile of the layout (eight compute
-// warps, 16 columns each) and a contiguous chunk of K. A producer thread
-// streams the chunk through a shared-memory ring in stages of four 64-k
-// blocks with exactly three copies per stage: one 16 KB bulk copy of the
-// weights (four consecutive tile-layout blocks), one bulk copy of their
-// scales and one 3-D TMA box of the activation rows (zero past M). Issuing a
-// copy costs a few hundred cycles whatever its size, so large stages are what
-// keep enough HBM traffic in flight. A thread-block cluster spans the K
-// chunks of the same columns; its CTAs reduce their partial sums through
-// distributed shared memory in rank order (deterministic, no global scratch).
+// warps, 16 columns each) and a contiguous slice of K. A producer thread
+// streams the slice through a shared-memory ring of STAGES stages, each four
+// 64-k blocks fetched with three copies: one bulk copy of the weights (four
+// consecutive tile-layout blocks, 16 KB), one of their scales and one 3-D TMA
+// box of the activation rows (zero past M). A deep ring keeps enough weight
+// bytes in flight per SM to stream HBM at full rate without holding them in
+// registers. A thread-block cluster spans the K slices of one column tile;
+// its CTAs reduce their partial sums through distributed shared memory, each
+// CTA summing a share of the tile over the ranks in rank order
+// (deterministic, no global scratch).
 #include "ptx.cuh"
 #include "gemm_tc.h"
 
 #include <cuda_runtime.h>
 
+#include <cstdlib>
+
 namespace i4g {
 namespace dec {
 
 constexpr int BK = 64;
-constexpr int KPS = 4;         // 64-k blocks per ring stage
-constexpr int STAGES = 2;
+constexpr int KPS = 4;  // 64-k blocks per ring stage
 constexpr int MAX_CLUSTER = 8;
 constexpr int NCOL = 128;
-constexpr int WARPS = NCOL / 16;
-constexpr int THREADS = (WARPS + 1) * 32;
-
-__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                          uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
-      "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
+constexpr int CWARPS = NCOL / 16;
+constexpr int THREADS = (CWARPS + 1) * 32;
+constexpr int CTAS_PER_SM = 2;
+constexpr int SMEM_PER_SM = 227 * 1024;
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -73,29 +68,177 @@ __device__ __forceinline__ float ld_dsmem_f32(uint32_t local_addr, uint32_t rank
   return v;
 }
 
-template <int MT, int GROUP>
+// One lane's share of one 64-k block: loads its weight words (column r0 at
+// wp, column r0 + 8 at wp + 128), the two columns' scales (sp, sp + 16) and
+// its activation chunks, decodes the 32 weights to exact half(q * s) and
+// issues the MMA steps. Decode of word w, pair p (k pair 2p, 2p+1 at bits 4p
+// and 16 + 4p): pairs 0 and 2 (of w and w >> 8) XOR the masked nibbles into
+// 0x6408, the half 1032 + q, then one exact subtraction of 1032; pairs 1 and 3
+// into 0x6480 = 1024 + 16 (q + 8), then one exact fma by 1/16 and -72. One
+// rounding multiply by the scale follows (explicit .rn: never contracted).
+// X is a register-name suffix, so that two blocks can share one asm
+// statement and interleave.
+#define I4G_DEC_REGS(X)                                                          \
+  ".reg .b32 w0" X ", w1" X ", w2" X ", w3" X ", y0" X ", y1" X ", y2" X ", y3" X \
+  ", s0" X ", s1" X ";\n\t"                                                      \
+  ".reg .b16 h0" X ", h1" X ";\n\t"                                              \
+  ".reg .b32 p0" X ", p1" X ", p2" X ", p3" X ", p4" X ", p5" X ", p6" X ", p7" X  \
+  ";\n\t"                                                                        \
+  ".reg .b32 q0" X ", q1" X ", q2" X ", q3" X ", q4" X ", q5" X ", q6" X ", q7" X  \
+  ";\n\t"                                                                        \
+  ".reg .b32 a0" X ", a1" X ", a2" X ", a3" X ", a4" X ", a5" X ", a6" X ", a7" X  \
+  ";\n\t"
+
+#define I4G_DEC_LOADS(X, WP, WOFS, SP, AP0, AP1, AOFS)                  \
+  "ld.shared.v2.b32 {w0" X ", w1" X "}, [" WP "+" WOFS "];\n\t"        \
+  "ld.shared.v2.b32 {w2" X ", w3" X "}, [" WP "+" WOFS "+128];\n\t"    \
+  "ld.shared.b16 h0" X ", [" SP "];\n\t"                               \
+  "ld.shared.b16 h1" X ", [" SP "+16];\n\t"                            \
+  "ld.shared.v4.b32 {a0" X ", a1" X ", a2" X ", a3" X "}, [" AP0 "+" AOFS "];\n\t" \
+  "ld.shared.v4.b32 {a4" X ", a5" X ", a6" X ", a7" X "}, [" AP1 "+" AOFS "];\n\t" \
+  "mov.b32 s0" X ", {h0" X ", h0" X "};\n\t"                            \
+  "mov.b32 s1" X ", {h1" X ", h1" X "};\n\t"
+
+#define I4G_DEC_WORD(W, T, O0, O1, O2, O3, S)                          \
+  "shr.b32 " T ", " W ", 8;\n\t"                                       \
+  "lop3.b32 " O0 ", " W ", 0x000F000F, 0x64086408, 0x6a;\n\t"          \
+  "lop3.b32 " O1 ", " W ", 0x00F000F0, 0x64806480, 0x6a;\n\t"          \
+  "lop3.b32 " O2 ", " T ", 0x000F000F, 0x64086408, 0x6a;\n\t"          \
+  "lop3.b32 " O3 ", " T ", 0x00F000F0, 0x64806480, 0x6a;\n\t"          \
+  "sub.rn.f16x2 " O0 ", " O0 ", kbias;\n\t"                            \
+  "fma.rn.f16x2 " O1 ", " O1 ", k16th, km72;\n\t"                      \
+  "sub.rn.f16x2 " O2 ", " O2 ", kbias;\n\t"                            \
+  "fma.rn.f16x2 " O3 ", " O3 ", k16th, km72;\n\t"                      \
+  "mul.rn.f16x2 " O0 ", " O0 ", " S ";\n\t"                            \
+  "mul.rn.f16x2 " O1 ", " O1 ", " S ";\n\t"                            \
+  "mul.rn.f16x2 " O2 ", " O2 ", " S ";\n\t"                            \
+  "mul.rn.f16x2 " O3 ", " O3 ", " S ";\n\t"
+
+#define I4G_DEC_DECODE(X)                                                                   \
+  I4G_DEC_WORD("w0" X, "y0" X, "p0" X, "p1" X, "p2" X, "p3" X, "s0" X)                      \
+  I4G_DEC_WORD("w1" X, "y1" X, "p4" X, "p5" X, "p6" X, "p7" X, "s0" X)                      \
+  I4G_DEC_WORD("w2" X, "y2" X, "q0" X, "q1" X, "q2" X, "q3" X, "s1" X)                      \
+  I4G_DEC_WORD("w3" X, "y3" X, "q4" X, "q5" X, "q6" X, "q7" X, "s1" X)
+
+// The four MMA steps of a block go to four independent accumulators, so a
+// warp issues them back to back instead of waiting on each result.
+#define I4G_DEC_MMA1(C, X, P, Q, B0, B1)                                                      \
+  "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {" C "}, {p" P X ", q" P X ", p" Q X   \
+  ", q" Q X "}, {" B0 ", " B1 "}, {" C "};\n\t"
+#define I4G_DEC_MMA(C0, C1, C2, C3, X, A)                                                     \
+  I4G_DEC_MMA1(C0, X, "0", "1", A "0" X, A "1" X)                                             \
+  I4G_DEC_MMA1(C1, X, "2", "3", A "2" X, A "3" X)                                             \
+  I4G_DEC_MMA1(C2, X, "4", "5", A "4" X, A "5" X)                                             \
+  I4G_DEC_MMA1(C3, X, "6", "7", A "6" X, A "7" X)
+
+#define I4G_DEC_CONSTS                                 \
+  ".reg .b32 kbias, k16th, km72;\n\t"                  \
+  "mov.b32 kbias, 0x64086408;\n\t"                     \
+  "mov.b32 k16th, 0x2C002C00;\n\t"                     \
+  "mov.b32 km72, 0xD480D480;\n\t"
+
+#define I4G_ACC16(A)                                                                        \
+  "+f"(A[0][0]), "+f"(A[0][1]), "+f"(A[0][2]), "+f"(A[0][3]), "+f"(A[1][0]), "+f"(A[1][1]),  \
+      "+f"(A[1][2]), "+f"(A[1][3]), "+f"(A[2][0]), "+f"(A[2][1]), "+f"(A[2][2]),             \
+      "+f"(A[2][3]), "+f"(A[3][0]), "+f"(A[3][1]), "+f"(A[3][2]), "+f"(A[3][3])
+
+// One block, 8 activation rows.
+__device__ __forceinline__ void block_step(uint32_t wp, uint32_t sp, uint32_t ap0, uint32_t ap1,
+                                           float (&acc)[1][4][4]) {
+  asm volatile(
+      "{\n\t" I4G_DEC_CONSTS I4G_DEC_REGS("A")
+      I4G_DEC_LOADS("A", "%16", "0", "%17", "%18", "%19", "0")
+      I4G_DEC_DECODE("A")
+      I4G_DEC_MMA("%0, %1, %2, %3", "%4, %5, %6, %7", "%8, %9, %10, %11", "%12, %13, %14, %15",
+                  "A", "a")
+      "}\n"
+      : I4G_ACC16(acc[0])
+      : "r"(wp), "r"(sp), "r"(ap0), "r"(ap1));
+}
+
+// Two consecutive blocks (weights 4096 bytes apart, activations 8 rows x 128
+// bytes apart), 8 activation rows: two independent decode streams in one
+// statement, so the scheduler can overlap them.
+__device__ __forceinline__ void block_step2(uint32_t wp, uint32_t sp0, uint32_t sp1, uint32_t ap0,
+                                            uint32_t ap1, float (&acc)[1][4][4]) {
+  asm volatile(
+      "{\n\t" I4G_DEC_CONSTS I4G_DEC_REGS("A") I4G_DEC_REGS("B")
+      I4G_DEC_LOADS("A", "%16", "0", "%17", "%19", "%20", "0")
+      I4G_DEC_LOADS("B", "%16", "4096", "%18", "%19", "%20", "1024")
+      I4G_DEC_DECODE("A")
+      I4G_DEC_DECODE("B")
+      I4G_DEC_MMA("%0, %1, %2, %3", "%4, %5, %6, %7", "%8, %9, %10, %11", "%12, %13, %14, %15",
+                  "A", "a")
+      I4G_DEC_MMA("%0, %1, %2, %3", "%4, %5, %6, %7", "%8, %9, %10, %11", "%12, %13, %14, %15",
+                  "B", "a")
+      "}\n"
+      : I4G_ACC16(acc[0])
+      : "r"(wp), "r"(sp0), "r"(sp1), "r"(ap0), "r"(ap1));
+}
+
+// One block, 16 activation rows: the second 8 rows sit 8 * 128 bytes further.
+__device__ __forceinline__ void block_step(uint32_t wp, uint32_t sp, uint32_t ap0, uint32_t ap1,
+                                           float (&acc)[2][4][4]) {
+  asm volatile(
+      "{\n\t" I4G_DEC_CONSTS I4G_DEC_REGS("A")
+      ".reg .b32 a0C, a1C, a2C, a3C, a4C, a5C, a6C, a7C;\n\t"
+      I4G_DEC_LOADS("A", "%32", "0", "%33", "%34", "%35", "0")
+      "ld.shared.v4.b32 {a0C, a1C, a2C, a3C}, [%34+1024];\n\t"
+      "ld.shared.v4.b32 {a4C, a5C, a6C, a7C}, [%35+1024];\n\t"
+      I4G_DEC_DECODE("A")
+      I4G_DEC_MMA("%0, %1, %2, %3", "%4, %5, %6, %7", "%8, %9, %10, %11", "%12, %13, %14, %15",
+                  "A", "a")
+      I4G_DEC_MMA1("%16, %17, %18, %19", "A", "0", "1", "a0C", "a1C")
+      I4G_DEC_MMA1("%20, %21, %22, %23", "A", "2", "3", "a2C", "a3C")
+      I4G_DEC_MMA1("%24, %25, %26, %27", "A", "4", "5", "a4C", "a5C")
+      I4G_DEC_MMA1("%28, %29, %30, %31", "A", "6", "7", "a6C", "a7C")
+      "}\n"
+      : I4G_ACC16(acc[0]), I4G_ACC16(acc[1])
+      : "r"(wp), "r"(sp), "r"(ap0), "r"(ap1));
+}
+
+#undef I4G_ACC16
+#undef I4G_DEC_CONSTS
+#undef I4G_DEC_MMA
+#undef I4G_DEC_MMA1
+#undef I4G_DEC_DECODE
+#undef I4G_DEC_WORD
+#undef I4G_DEC_LOADS
+#undef I4G_DEC_REGS
+
+template <int MT, int GROUP, int STAGES>
 struct Layout {
   static constexpr int ROWS = MT * 8;
-  static constexpr int ABYTES = KPS * ROWS * BK * 2;     // [KPS][ROWS][64] halves, swizzled
-  static constexpr int WBYTES = KPS * 4096;              // four tile-layout blocks
+  static constexpr int ABYTES = KPS * ROWS * BK * 2;  // [KPS][ROWS][64] halves, swizzled
+  static constexpr int WBYTES = KPS * 4096;           // four tile-layout blocks
   // scale groups a stage can touch (one more when a group spans two blocks
-  // and the chunk starts in the middle of one)
+  // and the slice starts in the middle of one)
   static constexpr int SGROUPS = KPS * BK / GROUP + (GROUP > BK ? 1 : 0);
   static constexpr int SBYTES = SGROUPS * 128 * 2;
   static constexpr int SLOT = ((ABYTES + WBYTES + SBYTES + 1023) / 1024) * 1024;
-  static constexpr int BARS = STAGES * SLOT;              // full[], empty[]
-  static constexpr int PARTIAL = BARS + 2 * STAGES * 8;   // fp32 partial tiles
-  static constexpr int ABORT = PARTIAL + WARPS * 32 * 4 * MT * 4;
-  static constexpr int DYN = ABORT + 16 + 1024;           // + slack for 1024B alignment
+  static constexpr int BARS = STAGES * SLOT;             // full[], empty[]
+  static constexpr int PARTIAL = BARS + 2 * STAGES * 8;  // fp32 partial tile
+  static constexpr int ABORT = PARTIAL + CWARPS * 32 * 4 * MT * 4;
+  static constexpr int DYN = ABORT + 16 + 1024;  // + slack for 1024-byte alignment
 };
 
+// Ring depth: as many stages as two CTAs per SM can hold, at most 6.
 template <int MT, int GROUP>
-__global__ void __launch_bounds__(THREADS, 2)
+constexpr int stages_for() {
+  int s = 6;
+  while (s > 2 && CTAS_PER_SM * (Layout<MT, GROUP, 6>::SLOT * s + 2 * s * 8 +
+                                 CWARPS * 32 * 4 * MT * 4 + 16 + 1024 + 1024) > SMEM_PER_SM)
+    --s;
+  return s;
+}
+
+template <int MT, int GROUP, int STAGES>
+__global__ void __launch_bounds__(THREADS, CTAS_PER_SM)
     decode_kernel(const __grid_constant__ CUtensorMap act_map,
                   const uint8_t* __restrict__ tiles, const __half* __restrict__ scales,
                   __half* __restrict__ c, int M, int N, int K, int* status,
                   unsigned long long wait_limit_ns) {
-  using L = Layout<MT, GROUP>;
+  using L = Layout<MT, GROUP, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -118,7 +261,7 @@ __global__ void __launch_bounds__(THREADS, 2)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(bars + 8 * s, 1);
-      mbar_init(bars + 8 * (STAGES + s), WARPS);
+      mbar_init(bars + 8 * (STAGES + s), CWARPS);
     }
     *abort_flag = 0;
     fence_mbarrier_init();
@@ -126,7 +269,7 @@ __global__ void __launch_bounds__(THREADS, 2)
   }
   __syncthreads();
 
-  if (warp == WARPS) {
+  if (warp == CWARPS) {
     // --------------------------------------------------------------- producer
     if (lane == 0) {
       prefetch_tensormap(&act_map);
@@ -145,8 +288,8 @@ __global__ void __launch_bounds__(THREADS, 2)
         const uint32_t dst = ring + s * L::SLOT;
         const uint32_t full = bars + 8 * s;
         mbar_arrive_expect_tx(full, L::ABYTES + nkb * 4096 + (g1 - g0) * 256);
-        tma_load_3d(dst, &act_map, full, 0, 0, kb);
         bulk_load(dst + L::ABYTES, wsrc + static_cast<size_t>(kb) * 4096, nkb * 4096, full);
+        tma_load_3d(dst, &act_map, full, 0, 0, kb);
         bulk_load(dst + L::ABYTES + L::WBYTES, ssrc + static_cast<size_t>(g0) * 128,
                   (g1 - g0) * 256, full);
       }
@@ -160,12 +303,15 @@ __global__ void __launch_bounds__(THREADS, 2)
     // ---------------------------------------------------------------- compute
     const int g = lane >> 2, t = lane & 3;
     const int r0 = warp * 16 + g;  // weight column (inside the tile) of a0/a2
-    float acc[MT][4];
+    float acc[MT][4][4];  // [row block][MMA step][fragment]
 #pragma unroll
     for (int mb = 0; mb < MT; ++mb)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) acc[mb][i] = 0.0f;
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[mb][q][i] = 0.0f;
     const uint32_t wofs = L::ABYTES + (t >> 1) * 2048 + r0 * 16 + (t & 1) * 8;
+    const uint32_t sofs = L::ABYTES + L::WBYTES + r0 * 2;
     // activation row (mb*8 + g) of block j: box row R = j*ROWS + mb*8 + g, and
     // R % 8 == g; 16-byte chunks 2t, 2t+1 sit at (chunk ^ g) under the swizzle
     const uint32_t aofs0 = g * 128 + (((2 * t) ^ g) << 4);
@@ -177,50 +323,25 @@ __global__ void __launch_bounds__(THREADS, 2)
       const uint32_t slot = ring + s * L::SLOT;
       const int kb = kb0 + i * KPS;
       const int nkb = min(KPS, kb1 - kb);
-      const int sg0 = kb * BK / GROUP;  // first scale group held by this stage
+      // scale group of this lane's 16 k in block j, relative to the stage's first
+      const int klane = kb * BK + 16 * t;
+      const int sg0 = kb * BK / GROUP;
+      const uint32_t sbase = slot + sofs;
+      int j = 0;
+      if constexpr (MT == 1) {
 #pragma unroll 1
-      for (int j = 0; j < nkb; ++j) {
-        uint32_t lo0, lo1, hi0, hi1;
-        uint16_t slo, shi;
-        const uint32_t wp = slot + j * 4096 + wofs;
-        asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(lo0), "=r"(lo1) : "r"(wp));
-        asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(hi0), "=r"(hi1) : "r"(wp + 128));
-        const int grp = ((kb + j) * BK + 16 * t) / GROUP - sg0;
-        const uint32_t sp = slot + L::ABYTES + L::WBYTES + (grp * 128 + r0) * 2;
-        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(slo) : "r"(sp));
-        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(shi) : "r"(sp + 16));
-        uint32_t av[MT][8];
-#pragma unroll
-        for (int mb = 0; mb < MT; ++mb) {
-          const uint32_t rb = slot + (j * L::ROWS + mb * 8) * 128;
-          asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-                       : "=r"(av[mb][0]), "=r"(av[mb][1]), "=r"(av[mb][2]), "=r"(av[mb][3])
-                       : "r"(rb + aofs0));
-          asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-                       : "=r"(av[mb][4]), "=r"(av[mb][5]), "=r"(av[mb][6]), "=r"(av[mb][7])
-                       : "r"(rb + aofs1));
+        for (; j + 2 <= nkb; j += 2) {
+          const uint32_t ab = slot + j * (L::ROWS * 128);
+          const uint32_t sp0 = sbase + ((klane + j * BK) / GROUP - sg0) * 256;
+          const uint32_t sp1 = sbase + ((klane + (j + 1) * BK) / GROUP - sg0) * 256;
+          block_step2(slot + wofs + j * 4096, sp0, sp1, ab + aofs0, ab + aofs1, acc);
         }
-        const uint32_t slo2 = half_bits_x2(slo), shi2 = half_bits_x2(shi);
-        const uint32_t lo[2] = {lo0, lo1}, hi[2] = {hi0, hi1};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint32_t wl = lo[q >> 1], wh = hi[q >> 1];
-          uint32_t a0, a1, a2, a3;
-          if (q & 1) {
-            a0 = decode_pair<2>(wl, slo2);
-            a2 = decode_pair<3>(wl, slo2);
-            a1 = decode_pair<2>(wh, shi2);
-            a3 = decode_pair<3>(wh, shi2);
-          } else {
-            a0 = decode_pair<0>(wl, slo2);
-            a2 = decode_pair<1>(wl, slo2);
-            a1 = decode_pair<0>(wh, shi2);
-            a3 = decode_pair<1>(wh, shi2);
-          }
-#pragma unroll
-          for (int mb = 0; mb < MT; ++mb)
-            mma_16816(acc[mb], a0, a1, a2, a3, av[mb][2 * q], av[mb][2 * q + 1]);
-        }
+      }
+#pragma unroll 1
+      for (; j < nkb; ++j) {
+        const uint32_t ab = slot + j * (L::ROWS * 128);
+        const uint32_t sp = sbase + ((klane + j * BK) / GROUP - sg0) * 256;
+        block_step(slot + wofs + j * 4096, sp, ab + aofs0, ab + aofs1, acc);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(bars + 8 * (STAGES + s));
@@ -228,37 +349,42 @@ __global__ void __launch_bounds__(THREADS, 2)
 #pragma unroll
     for (int mb = 0; mb < MT; ++mb)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) partial[(warp * 32 + lane) * 4 * MT + 4 * mb + i] = acc[mb][i];
+      for (int i = 0; i < 4; ++i)
+        partial[(threadIdx.x * MT + mb) * 4 + i] =
+            (acc[mb][0][i] + acc[mb][1][i]) + (acc[mb][2][i] + acc[mb][3][i]);
   }
 
-  // Cluster reduction over the K chunks, in rank order, by rank 0. The
-  // producer warp's lanes reconverge first: the cluster barrier is warp-aligned.
+  // Cluster reduction over the K slices: CTA `crank` sums its share of the
+  // tile's partial elements over ranks 0..csize-1 in rank order. The
+  // producer warp's lanes reconverge first: the cluster barrier is
+  // warp-aligned.
   __syncwarp();
   cluster_sync();
-  if (crank == 0 && warp < WARPS) {
-    const int g = lane >> 2, t = lane & 3;
-#pragma unroll
-    for (int mb = 0; mb < MT; ++mb)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int idx = (warp * 32 + lane) * 4 * MT + 4 * mb + i;
-        float sum = partial[idx];
-        const uint32_t addr = smem_u32(&partial[idx]);
-        for (uint32_t r = 1; r < csize; ++r) sum += ld_dsmem_f32(addr, r);
-        const int col = nt * NCOL + warp * 16 + g + ((i >> 1) << 3);
-        const int m = mb * 8 + 2 * t + (i & 1);
-        if (m < M) c[static_cast<size_t>(m) * N + col] = __float2half_rn(sum);
-      }
+  constexpr int ELEMS = CWARPS * 32 * MT * 4;
+  const int e0 = static_cast<int>((static_cast<long>(crank) * ELEMS) / csize);
+  const int e1 = static_cast<int>((static_cast<long>(crank + 1) * ELEMS) / csize);
+  const uint32_t part_u32 = smem_u32(partial);
+  for (int e = e0 + static_cast<int>(threadIdx.x); e < e1; e += THREADS) {
+    float sum = ld_dsmem_f32(part_u32 + e * 4, 0);
+    for (uint32_t r = 1; r < csize; ++r) sum += ld_dsmem_f32(part_u32 + e * 4, r);
+    const int i = e & 3;
+    const int mb = (e >> 2) % MT;
+    const int th = (e >> 2) / MT;
+    const int w = th >> 5, ln = th & 31;
+    const int col = nt * NCOL + w * 16 + (ln >> 2) + ((i >> 1) << 3);
+    const int m = mb * 8 + 2 * (ln & 3) + (i & 1);
+    if (m < M) c[static_cast<size_t>(m) * N + col] = __float2half_rn(sum);
   }
-  cluster_sync();  // every CTA's shared memory stays alive until rank 0 has read it
+  cluster_sync();  // every CTA's shared memory stays alive until all have read it
 }
 
 template <int MT, int GROUP>
 cudaError_t launch_typed(const CUtensorMap& act_map, const uint8_t* tiles, const __half* scales,
                          __half* c, int M, int N, int K, int cluster, int* status,
                          unsigned long long wait_limit_ns, cudaStream_t stream) {
-  using L = Layout<MT, GROUP>;
-  auto kernel = decode_kernel<MT, GROUP>;
+  constexpr int S = stages_for<MT, GROUP>();
+  using L = Layout<MT, GROUP, S>;
+  auto kernel = decode_kernel<MT, GROUP, S>;
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -282,16 +408,39 @@ cudaError_t launch_typed(const CUtensorMap& act_map, const uint8_t* tiles, const
                             wait_limit_ns);
 }
 
-// Cluster size: enough CTAs for about three per SM, each streaming at least
-// two ring stages.
+// Tuning override for the cluster size (1-8), read once from
+// I4G_DECODE_CLUSTER; 0 means the shape-based choice.
+int cluster_override() {
+  static const int v = [] {
+    const char* e = std::getenv("I4G_DECODE_CLUSTER");
+    const int c = e ? std::atoi(e) : 0;
+    return (c >= 1 && c <= MAX_CLUSTER) ? c : 0;
+  }();
+  return v;
+}
+
+// Cluster size: the K split that spreads the column tiles over the SMs most
+// evenly in one wave of resident CTAs (the busiest SM holds ceil(ctas / sms)
+// CTAs; the score is the mean over that), the larger split on ties, while
+// every CTA keeps at least two ring stages of work.
 int choose_cluster(int N, int K, int sm_count) {
+  if (cluster_override()) return cluster_override();
   const int kblocks = K / BK;
-  const int cols = N / NCOL;
-  int cluster = 1;
-  while (cluster < MAX_CLUSTER && cols * cluster < 3 * sm_count &&
-         kblocks / (cluster * 2) >= 2 * KPS)
-    cluster *= 2;
-  return cluster;
+  const int tiles = N / NCOL;
+  int best = 1;
+  double best_score = -1.0;
+  for (int cl = 1; cl <= MAX_CLUSTER; ++cl) {
+    if (cl > 1 && kblocks / cl < 2 * KPS) break;
+    const long ctas = static_cast<long>(tiles) * cl;
+    const long most = (ctas + sm_count - 1) / sm_count;
+    if (most > CTAS_PER_SM) break;
+    const double score = (static_cast<double>(ctas) / sm_count) / most;
+    if (score >= best_score - 1e-9) {
+      best_score = score;
+      best = cl;
+    }
+  }
+  return best;
 }
 
 template <int MT>
@@ -312,6 +461,12 @@ cudaError_t launch_mt(const CUtensorMap& act_map, const uint8_t* tiles, const __
 }
 
 int rows_for(int M) { return M <= 8 ? 8 : 16; }
+
+bool supported(int M, int K, int group) {
+  (void)K;
+  (void)group;
+  return M >= 1 && M <= MAX_M;
+}
 
 cudaError_t launch(const CUtensorMap& act_map, const uint8_t* tiles, const __half* scales,
                    __half* c, int M, int N, int K, int group, int sm_count, int* status,

@@ -29,6 +29,8 @@ cudaError_t launch(const CUtensorMap& act_map, int tile_m, const uint8_t* tiles,
 
 namespace dec {
 constexpr int MAX_M = 16;
+// Whether the decode kernel serves this M, K, group.
+bool supported(int M, int K, int group);
 // Rows of the activation box the decode kernel's tensor map must use.
 int rows_for(int M);
 cudaError_t launch(const CUtensorMap& act_map, const uint8_t* tiles, const __half* scales,
