@@ -60,11 +60,14 @@ __device__ __forceinline__ void cluster_sync() {
                ::: "memory");
 }
 
-__device__ __forceinline__ float ld_dsmem_f32(uint32_t local_addr, uint32_t rank) {
+__device__ __forceinline__ float4 ld_dsmem_f32x4(uint32_t local_addr, uint32_t rank) {
   uint32_t remote;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(remote)
+               : "memory");
   return v;
 }
 
@@ -206,6 +209,16 @@ __device__ __forceinline__ void block_step(uint32_t wp, uint32_t sp, uint32_t ap
 #undef I4G_DEC_LOADS
 #undef I4G_DEC_REGS
 
+// Byte offset, inside a stage's scales, of the group holding lane (., t)'s
+// 16 k of block j; `odd` is the parity of the stage's first block (a group
+// of 128 spans two blocks).
+template <int GROUP>
+__device__ __forceinline__ uint32_t scale_offset(int j, int t, int odd) {
+  if constexpr (GROUP == 32) return static_cast<uint32_t>(2 * j + (t >> 1)) * 256u;
+  if constexpr (GROUP == 64) return static_cast<uint32_t>(j) * 256u;
+  return static_cast<uint32_t>((j + odd) >> 1) * 256u;
+}
+
 template <int MT, int GROUP, int STAGES>
 struct Layout {
   static constexpr int ROWS = MT * 8;
@@ -323,25 +336,28 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM)
       const uint32_t slot = ring + s * L::SLOT;
       const int kb = kb0 + i * KPS;
       const int nkb = min(KPS, kb1 - kb);
-      // scale group of this lane's 16 k in block j, relative to the stage's first
-      const int klane = kb * BK + 16 * t;
-      const int sg0 = kb * BK / GROUP;
-      const uint32_t sbase = slot + sofs;
-      int j = 0;
-      if constexpr (MT == 1) {
-#pragma unroll 1
-        for (; j + 2 <= nkb; j += 2) {
-          const uint32_t ab = slot + j * (L::ROWS * 128);
-          const uint32_t sp0 = sbase + ((klane + j * BK) / GROUP - sg0) * 256;
-          const uint32_t sp1 = sbase + ((klane + (j + 1) * BK) / GROUP - sg0) * 256;
-          block_step2(slot + wofs + j * 4096, sp0, sp1, ab + aofs0, ab + aofs1, acc);
+      const uint32_t wp = slot + wofs;
+      const uint32_t sp = slot + sofs;
+      const uint32_t ap0 = slot + aofs0, ap1 = slot + aofs1;
+      const int odd = kb & 1;
+      if (nkb == KPS) {
+        if constexpr (MT == 1) {
+          block_step2(wp, sp + scale_offset<GROUP>(0, t, odd), sp + scale_offset<GROUP>(1, t, odd),
+                      ap0, ap1, acc);
+          block_step2(wp + 2 * 4096, sp + scale_offset<GROUP>(2, t, odd),
+                      sp + scale_offset<GROUP>(3, t, odd), ap0 + 2 * L::ROWS * 128,
+                      ap1 + 2 * L::ROWS * 128, acc);
+        } else {
+#pragma unroll
+          for (int j = 0; j < KPS; ++j)
+            block_step(wp + j * 4096, sp + scale_offset<GROUP>(j, t, odd),
+                       ap0 + j * (L::ROWS * 128), ap1 + j * (L::ROWS * 128), acc);
         }
-      }
+      } else {
 #pragma unroll 1
-      for (; j < nkb; ++j) {
-        const uint32_t ab = slot + j * (L::ROWS * 128);
-        const uint32_t sp = sbase + ((klane + j * BK) / GROUP - sg0) * 256;
-        block_step(slot + wofs + j * 4096, sp, ab + aofs0, ab + aofs1, acc);
+        for (int j = 0; j < nkb; ++j)
+          block_step(wp + j * 4096, sp + scale_offset<GROUP>(j, t, odd),
+                     ap0 + j * (L::ROWS * 128), ap1 + j * (L::ROWS * 128), acc);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(bars + 8 * (STAGES + s));
@@ -360,20 +376,43 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM)
   // warp-aligned.
   __syncwarp();
   cluster_sync();
-  constexpr int ELEMS = CWARPS * 32 * MT * 4;
-  const int e0 = static_cast<int>((static_cast<long>(crank) * ELEMS) / csize);
-  const int e1 = static_cast<int>((static_cast<long>(crank + 1) * ELEMS) / csize);
+  constexpr int UNITS = CWARPS * 32 * MT;  // float4 partial units of the tile
+  const int x0 = static_cast<int>((crank * UNITS) / csize);
+  const int x1 = static_cast<int>(((crank + 1) * UNITS) / csize);
   const uint32_t part_u32 = smem_u32(partial);
-  for (int e = e0 + static_cast<int>(threadIdx.x); e < e1; e += THREADS) {
-    float sum = ld_dsmem_f32(part_u32 + e * 4, 0);
-    for (uint32_t r = 1; r < csize; ++r) sum += ld_dsmem_f32(part_u32 + e * 4, r);
-    const int i = e & 3;
-    const int mb = (e >> 2) % MT;
-    const int th = (e >> 2) / MT;
+  for (int x = x0 + static_cast<int>(threadIdx.x); x < x1; x += THREADS) {
+    // every rank's partial is loaded before any is added; the sum runs in
+    // rank order
+    float4 v[MAX_CLUSTER];
+#pragma unroll
+    for (int r = 0; r < MAX_CLUSTER; ++r)
+      if (r < static_cast<int>(csize))
+        v[r] = ld_dsmem_f32x4(part_u32 + x * 16, static_cast<uint32_t>(r));
+    float4 sum = v[0];
+#pragma unroll
+    for (int r = 1; r < MAX_CLUSTER; ++r) {
+      if (r < static_cast<int>(csize)) {
+        sum.x += v[r].x;
+        sum.y += v[r].y;
+        sum.z += v[r].z;
+        sum.w += v[r].w;
+      }
+    }
+    const int mb = x % MT;
+    const int th = x / MT;
     const int w = th >> 5, ln = th & 31;
-    const int col = nt * NCOL + w * 16 + (ln >> 2) + ((i >> 1) << 3);
-    const int m = mb * 8 + 2 * (ln & 3) + (i & 1);
-    if (m < M) c[static_cast<size_t>(m) * N + col] = __float2half_rn(sum);
+    const int col = nt * NCOL + w * 16 + (ln >> 2);
+    const int m = mb * 8 + 2 * (ln & 3);
+    // fragment k: column col + 8 (k >> 1), row m + (k & 1)
+    __half* c0 = c + static_cast<size_t>(m) * N + col;
+    if (m < M) {
+      c0[0] = __float2half_rn(sum.x);
+      c0[8] = __float2half_rn(sum.z);
+    }
+    if (m + 1 < M) {
+      c0[N] = __float2half_rn(sum.y);
+      c0[N + 8] = __float2half_rn(sum.w);
+    }
   }
   cluster_sync();  // every CTA's shared memory stays alive until all have read it
 }
