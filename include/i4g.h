@@ -111,6 +111,14 @@ int i4g_repack_umma(const uint8_t* packed, uint8_t* tiles,
 int i4g_inverse_repack_umma(const uint8_t* tiles, uint8_t* packed,
                             int K, int N, void* stream);
 
+/* One-pass quantize + repack (the one-shot path of src/main.cu:320-331,
+ * launch_quantize followed by the repacks, fused): B fp16 [K][N] ->
+ * tiles (i4g_repack_umma layout) + scales in the i4g_repack_scales_128 layout,
+ * reading B once. Bytes identical to i4g_quantize -> i4g_repack_umma +
+ * i4g_repack_scales_128. K % max(64, group) == 0, N % 128 == 0. */
+int i4g_quantize_repack(const void* b, uint8_t* tiles, void* scales_repacked,
+                        int K, int N, int group, void* stream);
+
 /* ---- fused GEMM (include/kernels.cuh:24-25, 81-83) ------------------------ */
 
 /* launch_final (kernels/gemm_final.cu:5-13): C fp16 [M][N] = A x dequant(B).

@@ -77,6 +77,14 @@ inline void launch_repack_umma(const uint8_t* packed, uint8_t* tiles, int K, int
   i4g_throw_if(i4g_repack_umma(packed, tiles, K, N, stream), "launch_repack_umma");
 }
 
+// New: launch_quantize + launch_repack_umma + launch_repack_scales_128 in one
+// pass over B (the one-shot path of src/main.cu:320-331).
+inline void launch_quantize_repack(const half* b, uint8_t* tiles, half* repacked_scales, int K,
+                                   int N, int group_size, cudaStream_t stream = nullptr) {
+  i4g_throw_if(i4g_quantize_repack(b, tiles, repacked_scales, K, N, group_size, stream),
+               "launch_quantize_repack");
+}
+
 inline void launch_final(const half* a, const uint8_t* b, const half* s, half* c, int M, int N,
                          int K, int group, cudaStream_t stream) {
   i4g_throw_if(i4g_gemm(a, b, s, c, M, N, K, group, stream), "launch_final");

@@ -51,6 +51,7 @@ class I4GError(RuntimeError):
 _SIGNATURES = {
     "i4g_quantize": [_vp, _vp, _vp, _i, _i, _i, _vp],
     "i4g_dequantize": [_vp, _vp, _vp, _i, _i, _i, _vp],
+    "i4g_quantize_repack": [_vp, _vp, _vp, _i, _i, _i, _vp],
     "i4g_repack_128x32": [_vp, _vp, _vp, _vp, _i, _i, _i, _vp],
     "i4g_inverse_repack_128x32": [_vp, _vp, _i, _i, _vp],
     "i4g_repack_mma_128x32": [_vp, _vp, _i, _i, _vp],
@@ -129,6 +130,14 @@ def _call(name: str, *args) -> None:
 def launch_quantize(b, packed, scales, K: int, N: int, group_size: int, stream=None) -> None:
     """include/quant.cuh:6-7. Codes/scales bit-identical to quantize_cpu."""
     _call("i4g_quantize", _ptr(b), _ptr(packed), _ptr(scales), K, N, group_size, _stream(stream))
+
+
+def launch_quantize_repack(b, tiles, scales_repacked, K: int, N: int, group_size: int,
+                           stream=None) -> None:
+    """One pass: launch_quantize + launch_repack_umma + launch_repack_scales_128
+    (the one-shot path of src/main.cu:320-331), reading B once."""
+    _call("i4g_quantize_repack", _ptr(b), _ptr(tiles), _ptr(scales_repacked), K, N, group_size,
+          _stream(stream))
 
 
 def launch_dequantize(packed, scales, b, K: int, N: int, group_size: int, stream=None) -> None:

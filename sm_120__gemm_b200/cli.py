@@ -26,7 +26,8 @@ import torch
 from . import (QuantizedLinear, launch_dequantize, launch_final, launch_final_fp32,
                launch_inverse_repack_128x32, launch_inverse_repack_umma, launch_quantize,
                launch_repack_128x32, launch_repack_mma_128x32, launch_repack_mma_pair_128x32,
-               launch_repack_scales_128, launch_repack_umma)
+               launch_repack_scales_128, launch_repack_umma, launch_quantize_repack,
+               launch_final_ws, workspace_for)
 
 CSV_HEADER = ("version,description,M,N,K,group_size,BM,BN,BK,warp_tile_m,warp_tile_n,stages,"
               "threads,registers_per_thread,smem_bytes,occupancy,cache_mode,median_ms,mean_ms,"
@@ -195,6 +196,13 @@ def benchmark(size, groups, warmup, iters, csv_path, m=None, n=None, k=None):
             launch_final(x.a, rep, rsc, x.c, M, N, K, g)
 
         te2e = timing(e2e, warmup, iters)
+        tqr = timing(lambda: launch_quantize_repack(x.b, rep, rsc, K, N, g), warmup, iters)
+
+        def e2e_fused():
+            launch_quantize_repack(x.b, rep, rsc, K, N, g)
+            launch_final(x.a, rep, rsc, x.c, M, N, K, g)
+
+        te2e_fused = timing(e2e_fused, warmup, iters)
         ref = cublas_ref(x)
         launch_final(x.a, x.lin.tiles, x.lin.scales, x.c, M, N, K, g)
         torch.cuda.synchronize()
@@ -209,7 +217,8 @@ def benchmark(size, groups, warmup, iters, csv_path, m=None, n=None, k=None):
               f"mma_repack={tmma['median_ms']:.4f}ms pair_repack={tpair['median_ms']:.4f}ms "
               f"umma_repack={tumma['median_ms']:.4f}ms dequant={td['median_ms']:.4f}ms "
               f"cublas={tg['median_ms']:.4f}ms separate_total={tsep['median_ms']:.4f}ms "
-              f"end_to_end={te2e['median_ms']:.4f}ms final={tf['median_ms']:.4f}ms "
+              f"quantize_repack={tqr['median_ms']:.4f}ms end_to_end={te2e['median_ms']:.4f}ms "
+              f"end_to_end_fused={te2e_fused['median_ms']:.4f}ms final={tf['median_ms']:.4f}ms "
               f"({tflops(tf['median_ms']):.1f} TFLOP/s) final_cold={tcold['median_ms']:.4f}ms")
 
         def row(version, desc, cache, t, notes="", tfl=0.0, err_=None, hbm=0.0):
@@ -233,8 +242,14 @@ def benchmark(size, groups, warmup, iters, csv_path, m=None, n=None, k=None):
                 "preprocess", tpair),
             row("repack_umma", "sm_100a tile layout (128 cols x 64 k) + scales", "preprocess",
                 tumma),
+            row("quantize_repack", "one-pass quantize into the sm_100a tile + scale layouts",
+                "preprocess", tqr, "bytes identical to quantize + repack_umma + scales",
+                hbm=gbs(tqr, 2 * K * N + K * N // 2 + 2 * N * (K // g))),
             row("end_to_end", "quantize + tile repack + fused final GEMM", "one-shot", te2e,
                 "preprocessing is normally amortized", tfl=tflops(te2e["median_ms"])),
+            row("end_to_end_fused", "one-pass quantize_repack + fused final GEMM", "one-shot",
+                te2e_fused, "preprocessing is normally amortized",
+                tfl=tflops(te2e_fused["median_ms"])),
             row("dequant", "materialize packed INT4 B as FP16", "baseline-component", td),
             row("cublas_fp16", "cuBLAS FP16 on dequantized B", "steady", tg,
                 "not workload-equivalent: B already materialized", tfl=tflops(tg["median_ms"])),
@@ -266,6 +281,11 @@ def profile_one(size, group, version, m=None, n=None, k=None, launches=1, warmup
     x = Case(M, N, K, group)
     if version == "final":
         fn = lambda: launch_final(x.a, x.lin.tiles, x.lin.scales, x.c, M, N, K, group)  # noqa
+    elif version == "final_ws":
+        ws = workspace_for(M, N, K)
+        fn = lambda: launch_final_ws(x.a, x.lin.tiles, x.lin.scales, x.c, M, N, K, group, ws)  # noqa
+    elif version == "quantize_repack":
+        fn = lambda: launch_quantize_repack(x.b, x.lin.tiles, x.lin.scales, K, N, group)  # noqa
     elif version == "quantize":
         fn = lambda: launch_quantize(x.b, x.packed, x.scales, K, N, group)  # noqa
     elif version == "repack_umma":

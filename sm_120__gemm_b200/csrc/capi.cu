@@ -325,6 +325,25 @@ int i4g_quantize(const void* b, uint8_t* packed, void* scales, int K, int N, int
                 "quantize launch");
 }
 
+int i4g_quantize_repack(const void* b, uint8_t* tiles, void* scales_repacked, int K, int N,
+                        int group, void* stream) {
+  if (!b || !tiles || !scales_repacked) return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
+  int st = check_group(K, group, true);
+  if (st != I4G_OK) return st;
+  const int kc = group > 64 ? group : 64;
+  if (K < kc || N < 128 || K % kc != 0 || N % 128 != 0)
+    return fail(I4G_ERR_SHAPE, "quantize_repack needs K %% %d == 0 and N %% 128 == 0 (K=%d N=%d)",
+                kc, K, N);
+  if (!aligned(b, 16) || !aligned(tiles, 16) || !aligned(scales_repacked, 2))
+    return fail(I4G_ERR_ALIGNMENT, "b and tiles must be 16-byte aligned");
+  DeviceInfo* dev = nullptr;
+  if ((st = current_device(&dev)) != I4G_OK) return st;
+  return finish(i4g::prep::quantize_repack(static_cast<const __half*>(b), tiles,
+                                           static_cast<__half*>(scales_repacked), K, N, group,
+                                           static_cast<cudaStream_t>(stream)),
+                "quantize_repack launch");
+}
+
 int i4g_dequantize(const uint8_t* packed, const void* scales, void* b, int K, int N, int group,
                    void* stream) {
   if (!b || !packed || !scales) return fail(I4G_ERR_NULL_POINTER, "null pointer argument");

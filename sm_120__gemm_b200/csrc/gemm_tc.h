@@ -39,6 +39,10 @@ cudaError_t launch(const CUtensorMap& act_map, const uint8_t* tiles, const __hal
 }  // namespace dec
 
 namespace prep {
+// quantize + repack_umma + repack_scales_128 in one pass over B.
+// K % max(64, group) == 0, N % 128 == 0.
+cudaError_t quantize_repack(const __half* b, uint8_t* tiles, __half* rscales, int K, int N,
+                            int group, cudaStream_t stream);
 cudaError_t quantize(const __half* b, uint8_t* packed, __half* scales, int K, int N, int group,
                      cudaStream_t stream);
 cudaError_t dequantize(const uint8_t* packed, const __half* scales, __half* b, int K, int N,

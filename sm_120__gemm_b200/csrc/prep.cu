@@ -254,7 +254,74 @@ __global__ void inverse_repack_umma_kernel(const uint32_t* __restrict__ tiles,
 
 inline unsigned blocks_for(size_t n) { return static_cast<unsigned>((n + THREADS - 1) / THREADS); }
 
+
+// One pass from FP16 weights to the GEMM's inputs: a CTA reads a 128-column
+// x KC-row slab of B once (KC = max(64, group), whole groups and whole tile
+// blocks), computes the slab's scales exactly as quantize_kernel does, and
+// writes the codes straight into the tile layout of repack_umma_kernel and
+// the scales into the 128-column layout of repack_scales_128_kernel. Output
+// bytes are identical to quantize -> repack_umma + repack_scales_128.
+template <int GROUP>
+__global__ void __launch_bounds__(THREADS)
+    quantize_repack_kernel(const __half* __restrict__ b, uint32_t* __restrict__ tiles,
+                           __half* __restrict__ rscales, int K, int N) {
+  constexpr int KC = GROUP > 64 ? GROUP : 64;
+  constexpr int GPC = KC / GROUP;  // groups per slab
+  __shared__ __align__(16) __half slab[KC][128];
+  __shared__ float sf[GPC][128];
+  const int nt = blockIdx.x;
+  const int kc = blockIdx.y;
+  const int k0 = kc * KC;
+  // B rows k0..k0+KC, columns 128 nt..: 16 chunks of 16 bytes per row
+  for (int i = threadIdx.x; i < KC * 16; i += THREADS) {
+    const int r = i >> 4, ch = i & 15;
+    *reinterpret_cast<uint4*>(&slab[r][ch * 8]) = *reinterpret_cast<const uint4*>(
+        b + static_cast<size_t>(k0 + r) * N + static_cast<size_t>(nt) * 128 + ch * 8);
+  }
+  __syncthreads();
+  const int groups = K / GROUP;
+  for (int i = threadIdx.x; i < GPC * 128; i += THREADS) {
+    const int gl = i >> 7, col = i & 127;
+    float vmax = 0.0f;
+    for (int r = gl * GROUP; r < (gl + 1) * GROUP; ++r)
+      vmax = max_like_std(vmax, fabsf(__half2float(slab[r][col])));
+    const __half sh = __float2half_rn(max_like_std(__fdiv_rn(vmax, 7.0f), 1.0e-8f));
+    rscales[(static_cast<size_t>(nt) * groups + kc * GPC + gl) * 128 + col] = sh;
+    sf[gl][col] = __half2float(sh);
+  }
+  __syncthreads();
+  // tile-layout words of the slab's KC / 64 blocks: block [h][n][w], element
+  // k % 8 = 2p + hi at bit 4p + 16hi
+  const int kblocks = K >> 6;
+  for (int i = threadIdx.x; i < (KC / 64) * 1024; i += THREADS) {
+    const int jb = i >> 10, wi = i & 1023;
+    const int h = wi >> 9, ni = (wi >> 2) & 127, w = wi & 3;
+    const int kk0 = jb * 64 + h * 32 + w * 8;  // row inside the slab
+    const float sc = sf[kk0 / GROUP][ni];
+    uint32_t word = 0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int q = quantize_one(__half2float(slab[kk0 + e][ni]), sc);
+      word |= static_cast<uint32_t>(q & 15) << (4 * (e >> 1) + 16 * (e & 1));
+    }
+    tiles[(static_cast<size_t>(nt) * kblocks + kc * (KC / 64) + jb) * 1024 + wi] = word;
+  }
+}
+
 }  // namespace
+
+cudaError_t quantize_repack(const __half* b, uint8_t* tiles, __half* rscales, int K, int N,
+                            int group, cudaStream_t stream) {
+  uint32_t* t = reinterpret_cast<uint32_t*>(tiles);
+  const int kc = group > 64 ? group : 64;
+  const dim3 grid(N / 128, K / kc);
+  switch (group) {
+    case 32: quantize_repack_kernel<32><<<grid, THREADS, 0, stream>>>(b, t, rscales, K, N); break;
+    case 64: quantize_repack_kernel<64><<<grid, THREADS, 0, stream>>>(b, t, rscales, K, N); break;
+    default: quantize_repack_kernel<128><<<grid, THREADS, 0, stream>>>(b, t, rscales, K, N); break;
+  }
+  return cudaGetLastError();
+}
 
 cudaError_t quantize(const __half* b, uint8_t* packed, __half* scales, int K, int N, int group,
                      cudaStream_t stream) {

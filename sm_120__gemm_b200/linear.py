@@ -9,7 +9,7 @@ from __future__ import annotations
 
 import torch
 
-from . import (launch_final_fp32_ws, launch_final_ws, launch_quantize,
+from . import (launch_final_fp32_ws, launch_final_ws, launch_quantize_repack,
                launch_repack_scales_128, launch_repack_umma, shard_range, workspace_for)
 
 
@@ -25,16 +25,17 @@ class QuantizedLinear:
     @classmethod
     def from_weight(cls, w: torch.Tensor, group: int, stream=None) -> "QuantizedLinear":
         """Quantise an fp16 [K, N] weight on the GPU (codes and scales
-        bit-identical to the reference's quantize_cpu) and repack it."""
+        bit-identical to the reference's quantize_cpu) straight into the GEMM
+        layouts, in one pass."""
         if w.dtype != torch.float16 or w.dim() != 2 or not w.is_cuda:
             raise TypeError("weight must be a 2-D float16 CUDA tensor [K, N]")
         w = w.contiguous()
         K, N = w.shape
         dev = w.device
-        packed = torch.empty(K * N // 2, dtype=torch.uint8, device=dev)
-        scales = torch.empty((K + group - 1) // group, N, dtype=torch.float16, device=dev)
-        launch_quantize(w, packed, scales, K, N, group, stream)
-        return cls.from_packed(packed, scales, K, N, group, stream)
+        tiles = torch.empty(K * N // 2, dtype=torch.uint8, device=dev)
+        rscales = torch.empty((K // group) * N, dtype=torch.float16, device=dev)
+        launch_quantize_repack(w, tiles, rscales, K, N, group, stream)
+        return cls(tiles, rscales, K, N, group)
 
     @classmethod
     def from_packed(cls, packed: torch.Tensor, scales: torch.Tensor, K: int, N: int,

@@ -231,3 +231,39 @@ def test_wait_timeout_is_reported_not_faulted(i4g):
     # the context is still usable
     rep, _ = run_case(i4g, 64, 128, 128, 32)
     assert rep["ok"], rep
+
+
+# ------------------------------------------------- one-pass quantize + repack
+
+def special_weights(K, N, seed):
+    """N(0, 0.02) weights with the quantiser's edge cases planted: an all-zero
+    group, subnormal and tie values, +-65504 and a lone large outlier."""
+    g = torch.Generator().manual_seed(seed)
+    w = torch.randn(K, N, generator=g) * 0.02
+    w[0:32, 0] = 0.0
+    w[0:32, 1] = 2.0 ** -20
+    w[:, 2] = torch.tensor([(-1) ** i * (i % 16) * 0.5 for i in range(K)])
+    w[5, 3] = 65504.0
+    w[6, 3] = -65504.0
+    w[7, 4] = 1.0e4
+    return w.half()
+
+
+@pytest.mark.parametrize("K,N,grp", [(64, 128, 32), (128, 256, 64), (256, 384, 128),
+                                     (4096, 1024, 32), (4096, 1024, 128), (1024, 4096, 64)])
+def test_quantize_repack_one_pass_matches_three_step(i4g, K, N, grp):
+    w = special_weights(K, N, K + N + grp).cuda()
+    tiles = torch.empty(K * N // 2, dtype=torch.uint8, device="cuda")
+    rsc = torch.empty((K // grp) * N, dtype=torch.float16, device="cuda")
+    i4g.launch_quantize_repack(w, tiles, rsc, K, N, grp)
+    packed, scales = gpu_quantize(i4g, u16(w.cpu()), K, N, grp)
+    lin = i4g.QuantizedLinear.from_packed(packed, scales, K, N, grp)
+    torch.cuda.synchronize()
+    assert torch.equal(tiles, lin.tiles)
+    assert torch.equal(rsc.view(torch.int16), lin.scales.view(torch.int16))
+    # and against the oracle's codes (through the inverse tile repack)
+    pk_np, sc_np = oracle.quantize(u16(w.cpu()), K, N, grp)
+    back = torch.empty(K * N // 2, dtype=torch.uint8, device="cuda")
+    i4g.launch_inverse_repack_umma(tiles, back, K, N)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(back.cpu().numpy(), pk_np)
