@@ -7,6 +7,7 @@ binary (src/main.cu:415-439): the same modes and options.
     python -m sm_120__gemm_b200.cli --benchmark --size 4096 --group all \
         --warmup 20 --iters 100 --csv results.csv
     python -m sm_120__gemm_b200.cli --profile final --size 4096 --group 128 [--m M --n N --k K]
+    python -m sm_120__gemm_b200.cli --configs [--iters 50] [--csv configs.csv]
 
 Correctness gates are the reference's (src/main.cu:257-261): against cuBLAS
 (torch.matmul) on the GPU-dequantised B, rel_l2 < 0.02 and max_abs < 2.0.
@@ -305,6 +306,150 @@ def profile_one(size, group, version, m=None, n=None, k=None, launches=1, warmup
     print(f"profiled {version} M={M} N={N} K={K} group={group}")
 
 
+def config_shapes():
+    """The shapes of the benchmark configurations on one GPU (a rank's slice
+    for the column-parallel ones): decode MLP linears, the 70B-class prefill
+    up-projection at G = 1/2/4/8, and the M sweep of the fused gate+up
+    projection (one of 8 ranks: N = 57344 / 8)."""
+    out = []
+    for (K, N) in ((4096, 14336), (14336, 4096)):
+        for M in (1, 4, 8, 16):
+            out.append(("decode", M, N, K, 128))
+    for G in (1, 2, 4, 8):
+        out.append((f"prefill G={G}", 8192, 28672 // G, 8192, 128))
+    for M in (1, 16, 128, 1024, 4096, 16384):
+        out.append(("m-sweep rank 1/8", M, 7168, 8192, 64))
+    return out
+
+
+def configs(iters, csv_path=""):
+    """Per shape: the kernel the dispatcher picks, the tcgen05 schedule, and
+    the device time per call through QuantizedLinear (split-K workspace
+    included), from a CUDA graph of back-to-back calls that rotate enough
+    weight and activation sets to keep their operands out of L2."""
+    pk_tf, pk_bw = peaks()
+    l2 = torch.cuda.get_device_properties(0).L2_cache_size
+    lines = ["config,M,N,K,group,kernel,schedule,us_per_call,tflops,algorithmic_gbs,"
+             "frac_tensor,frac_hbm"]
+    for (label, M, N, K, g) in config_shapes():
+        wbytes = K * N // 2
+        nw = max(1, min(8, -(-2 * l2 // wbytes)))
+        na = max(1, min(4, -(-2 * l2 // (2 * M * K))))
+        gen = torch.Generator(device="cuda").manual_seed(M * 131 + N * 7 + K)
+        lins = []
+        for _ in range(nw):
+            w = (torch.randn(K, N, generator=gen, device="cuda") * 0.02).half()
+            lins.append(QuantizedLinear.from_weight(w, g))
+            del w
+        acts = [(torch.rand(M, K, generator=gen, device="cuda") * 2 - 1).half() for _ in range(na)]
+        c = torch.empty(M, N, dtype=torch.float16, device="cuda")
+        ws = workspace_for(M, N, K)
+        side = torch.cuda.Stream()
+        for i in range(max(nw, na)):
+            lins[i % nw](acts[i % na], out=c)
+        torch.cuda.synchronize()
+        ws = workspace_for(M, N, K, stream=side)
+        side.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(graph, stream=side):
+                for i in range(iters):
+                    lins[i % nw](acts[i % na], out=c, stream=side)
+        torch.cuda.current_stream().wait_stream(side)
+        graph.replay()
+        torch.cuda.synchronize()
+        best = float("inf")
+        for _ in range(3):
+            b, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            b.record()
+            graph.replay()
+            e.record()
+            e.synchronize()
+            best = min(best, b.elapsed_time(e) * 1e3 / iters)
+        del graph
+        flops = 2.0 * M * N * K
+        nbytes = 2 * M * K + K * N // 2 + 2 * N * (K // g) + 2 * M * N
+        tf = flops / (best * 1e-6) / 1e12
+        gbs = nbytes / (best * 1e-6) / 1e9
+        kernel = "decode (mma.sync)" if M <= 16 else "tcgen05"
+        sched = "-" if M <= 16 else ("split-K tail" if ws is not None else "whole tiles")
+        lines.append(f"{label},{M},{N},{K},{g},{kernel},{sched},{best:.2f},{tf:.1f},{gbs:.0f},"
+                     f"{tf / pk_tf:.3f},{gbs / pk_bw:.3f}")
+        print(lines[-1], flush=True)
+        del lins, acts, c
+        torch.cuda.empty_cache()
+    if csv_path:
+        with open(csv_path, "w") as f:
+            f.write("\n".join(lines) + "\n")
+
+
+def gather_sweep(iters):
+    """The M sweep of the fused gate+up projection (K=8192, N=57344, g64),
+    column-parallel over the ranks of a torchrun job, each rank owning
+    N / world columns: per M, the GEMM alone and the GEMM plus the NCCL
+    all-gather of C (end to end), max over ranks of CUDA-event times."""
+    import datetime
+
+    import torch.distributed as dist
+
+    from .sharded import ColumnParallelLinear, gather_columns
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120), device_id=dev)
+    K, N, g = 8192, 57344, 64
+    n_local = N // world
+    try:
+        gen = torch.Generator(device=dev).manual_seed(9000 + rank)
+        w = (torch.randn(K, n_local, generator=gen, device=dev) * 0.02).half()
+        cp = ColumnParallelLinear(QuantizedLinear.from_weight(w, g), world, rank)
+        del w
+        if rank == 0:
+            print("M,world,kernel,gemm_us,gemm_plus_gather_us,gather_share")
+        for M in (1, 16, 128, 1024, 4096, 16384):
+            a = (torch.rand(M, K, generator=gen, device=dev) * 2 - 1).half()
+            c_local = torch.empty(M, n_local, dtype=torch.float16, device=dev)
+            gathered = torch.empty(world * M * n_local, dtype=torch.float16, device=dev)
+            out = torch.empty(M, N, dtype=torch.float16, device=dev)
+
+            def gemm():
+                cp.forward_local(a, out=c_local)
+
+            def e2e():
+                cp.forward_local(a, out=c_local)
+                if world > 1:
+                    gather_columns(c_local, out=out, gathered=gathered)
+
+            res = []
+            for fn in (gemm, e2e):
+                for _ in range(3):
+                    fn()
+                torch.cuda.synchronize()
+                dist.barrier()
+                b, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                b.record()
+                for _ in range(iters):
+                    fn()
+                e.record()
+                e.synchronize()
+                t = torch.tensor([b.elapsed_time(e) * 1e3 / iters], device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                res.append(float(t.item()))
+            if rank == 0:
+                kern = "decode" if M <= 16 else "tcgen05"
+                print(f"{M},{world},{kern},{res[0]:.2f},{res[1]:.2f},"
+                      f"{(res[1] - res[0]) / res[1]:.3f}", flush=True)
+            del a, c_local, gathered, out
+            torch.cuda.empty_cache()
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
 def hardware():
     print(f"torch {torch.__version__}, CUDA runtime {torch.version.cuda}")
     for d in range(torch.cuda.device_count()):
@@ -322,6 +467,8 @@ def main(argv=None):
     mode.add_argument("--fp32-output-check", action="store_true")
     mode.add_argument("--benchmark", action="store_true")
     mode.add_argument("--profile", metavar="VERSION")
+    mode.add_argument("--configs", action="store_true")
+    mode.add_argument("--gather-sweep", action="store_true")
     ap.add_argument("--size", type=int, default=256)
     ap.add_argument("--group", default="32")
     ap.add_argument("--warmup", type=int, default=20)
@@ -344,6 +491,10 @@ def main(argv=None):
             benchmark(a.size, groups, a.warmup, a.iters, a.csv, a.m, a.n, a.k)
         elif a.profile:
             profile_one(a.size, groups[0], a.profile, a.m, a.n, a.k, a.launches)
+        elif a.configs:
+            configs(a.iters, a.csv)
+        elif a.gather_sweep:
+            gather_sweep(a.iters)
         else:
             hardware()
     except Exception as e:  # the reference prints ERROR and exits 1 (main.cu:437)
