@@ -143,8 +143,10 @@ int i4g_gemm_variant(const void* A, const uint8_t* tiles, const void* scales,
 
 /* The tcgen05 kernel runs ceil(M/TILE_M) x N/128 output tiles on one CTA per
  * SM. When the tile count is not a multiple of the SM count, the *_ws entry
- * points split the tiles of the last, partial wave along K (2 to 4 ways) and
- * reduce their FP32 partial tiles through a caller-owned workspace, in a fixed
+ * points share the tiles of the last, partial wave out along K over all SMs
+ * (stream-K: equal shares of the leftover tiles' 64-k blocks, one per CTA;
+ * or, with a smaller workspace, each leftover tile split 2 to 4 ways) and
+ * reduce the FP32 partial tiles through a caller-owned workspace, in a fixed
  * order, so results are bitwise reproducible and within the usual FP32
  * accumulation tolerance of the unsplit kernel.
  *
@@ -154,8 +156,8 @@ int i4g_gemm_variant(const void* A, const uint8_t* tiles, const void* scales,
  * i4g_gemm_ws / i4g_gemm_fp32_ws: i4g_gemm / i4g_gemm_fp32 with a workspace.
  * workspace: 256-byte aligned device memory, ZEROED ONCE before its first use
  * (its first 1024 bytes are arrival counters that every launch returns to
- * zero). workspace == NULL or workspace_bytes smaller than needed runs the
- * unsplit schedule. Launches sharing one workspace must be ordered (one
+ * zero). A workspace smaller than i4g_gemm_workspace_size reports gets the
+ * best schedule that fits (equal splits, or whole tiles; NULL: whole tiles). Launches sharing one workspace must be ordered (one
  * stream); concurrent launches on the same workspace race. */
 int i4g_gemm_workspace_size(int M, int N, int K, size_t* bytes);
 int i4g_gemm_ws(const void* A, const uint8_t* tiles, const void* scales, void* C,
@@ -169,10 +171,10 @@ int i4g_gemm_fp32_ws(const void* A, const uint8_t* tiles, const void* scales,
 
 /* i4g_gemm_ws for callers that cannot allocate device memory or own a
  * workspace (e.g. a host framework whose memory is fully pooled, or a plugin
- * given only A, B and C): the split-K workspace is a fixed 20 MiB array in
+ * given only A, B and C): the split-K workspace is a fixed 40 MiB array in
  * static device memory, one per device, so nothing is allocated per call.
- * Limit: shapes whose split-K workspace exceeds 20 MiB are rejected with
- * I4G_ERR_SHAPE (none on a device with up to 159 SMs; B200 has 148).
+ * Limit: shapes whose split-K workspace exceeds 40 MiB are rejected with
+ * I4G_ERR_SHAPE (none on a device with up to 160 SMs; B200 has 148).
  * Set-up: the first call on a device loads the scratch and looks up its
  * address with that device current; make that call before any stream
  * capture. Each call clears the scratch's 1 KiB of arrival counters on

@@ -7,6 +7,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <cstdint>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -256,14 +257,13 @@ int gemm_common(const void* A, const uint8_t* tiles, const void* scales, void* C
                   "decode kernel launch");
   }
   const int tile_m = tc_tile_m(M, N, dev);
-  i4g::tc::Plan plan = i4g::tc::make_plan(tile_m, M, N, K, dev->sm_count, workspace != nullptr);
-  if (plan.workspace_bytes > workspace_bytes)
-    plan = i4g::tc::make_plan(tile_m, M, N, K, dev->sm_count, false);
+  const i4g::tc::Plan plan = i4g::tc::make_plan(tile_m, M, N, K, dev->sm_count,
+                                                workspace ? workspace_bytes : 0, true);
   const CUtensorMap* map = nullptr;
   st = act_map(A, M, K, tile_m, &map);
   if (st != I4G_OK) return st;
-  return finish(i4g::tc::launch(*map, tile_m, tiles, sc, C, fp32_out, M, N, K, group,
-                                dev->sm_count, plan, plan.split > 1 ? workspace : nullptr,
+  return finish(i4g::tc::launch(*map, tile_m, tiles, sc, C, fp32_out, M, N, K, group, plan,
+                                plan.workspace_bytes > 0 ? workspace : nullptr,
                                 dev->status_word, g_wait_limit_ns, s),
                 "tcgen05 kernel launch");
 }
@@ -487,7 +487,7 @@ int i4g_gemm_workspace_size(int M, int N, int K, size_t* bytes) {
   if ((st = current_device(&dev)) != I4G_OK) return st;
   // the decode kernel needs none (its largest-K limit is for group 32)
   if (i4g::dec::supported(M, K, 32)) return I4G_OK;
-  *bytes = i4g::tc::make_plan(tc_tile_m(M, N, dev), M, N, K, dev->sm_count, true)
+  *bytes = i4g::tc::make_plan(tc_tile_m(M, N, dev), M, N, K, dev->sm_count, SIZE_MAX, true)
                .workspace_bytes;
   return I4G_OK;
 }
@@ -513,7 +513,7 @@ int i4g_gemm_static_scratch(const void* A, const uint8_t* tiles, const void* sca
   if ((st = current_device(&dev)) != I4G_OK) return st;
   size_t need = 0;
   if (!i4g::dec::supported(M, K, group))
-    need = i4g::tc::make_plan(tc_tile_m(M, N, dev), M, N, K, dev->sm_count, true)
+    need = i4g::tc::make_plan(tc_tile_m(M, N, dev), M, N, K, dev->sm_count, SIZE_MAX, true)
                .workspace_bytes;
   if (need > i4g::static_scratch_bytes()) {
     std::snprintf(t_last_error, sizeof(t_last_error),

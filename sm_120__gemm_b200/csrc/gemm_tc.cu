@@ -33,12 +33,16 @@
 // The weight ring does not wait for the tensor core, so the dequant runs
 // ahead of the MMA by up to T_STAGES blocks.
 //
-// Schedule: work items are whole tiles, then (when the caller provides a
-// workspace) the tiles of the last, partial wave split along K into `split`
-// items each, so the last wave keeps every SM busy. A split item writes its
-// FP32 partial tile to the workspace and takes a ticket; the item that draws
-// the last ticket sums the partials in split order (deterministic) and writes
-// C, then resets the ticket counter for the next launch.
+// Schedule: work items are whole tiles, round robin over the grid; then,
+// when the caller provides a workspace, the tiles of the last, partial wave
+// ("tail") are shared out along K so that the last wave keeps every SM busy:
+// either each tail tile split into `split` equal items, or (stream-K) the
+// tail's run of (tile, 64-k block) blocks cut into `chunks` equal shares, one
+// per CTA, each share covering the end of one tile and the start of the
+// next. A partial item writes its FP32 partial tile to a workspace slot and
+// takes a ticket; the item that draws the tile's last ticket sums the tile's
+// partials in slot order (deterministic) and writes C, then resets the
+// ticket counter for the next launch.
 #include "ptx.cuh"
 #include "gemm_tc.h"
 
@@ -97,30 +101,70 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
 
 struct Item {
   int mt, nt, kb0, kb1;
-  int rem;  // index among the split tiles, or -1 for a whole tile
-  int f;    // K split index
+  int rem;        // index among the tail tiles, or -1 for a whole tile
+  int slot;       // workspace slot of this item's partial tile
+  int base_slot;  // first slot of the tile's partials (contiguous)
+  int nparts;     // partial items of the tile
 };
 
-__device__ __forceinline__ Item item_info(int item, int full_tiles, int split, int kblocks,
-                                          int num_m, int num_n) {
-  Item r;
+// Work of CTA `b` of a grid of `g`: its `j`-th item, false past its last.
+static __device__ __noinline__ bool next_item(const Sched& s, int b, int g, int j, int kblocks,
+                                          int num_m, int num_n, Item& r) {
   int tile;
-  if (item < full_tiles) {
-    tile = item;
-    r.kb0 = 0;
-    r.kb1 = kblocks;
-    r.rem = -1;
-    r.f = 0;
+  if (s.chunks == 0) {
+    // whole tiles, then `split` equal K splits of each tail tile
+    const int item = b + j * g;
+    if (item >= s.items) return false;
+    if (item < s.full_tiles) {
+      tile = item;
+      r.kb0 = 0;
+      r.kb1 = kblocks;
+      r.rem = -1;
+    } else {
+      const int q = item - s.full_tiles;
+      r.rem = q / s.split;
+      const int f = q - r.rem * s.split;
+      tile = s.full_tiles + r.rem;
+      r.kb0 = (f * kblocks) / s.split;
+      r.kb1 = ((f + 1) * kblocks) / s.split;
+      r.base_slot = r.rem * s.split;
+      r.slot = r.base_slot + f;
+      r.nparts = s.split;
+    }
   } else {
-    const int j = item - full_tiles;
-    r.rem = j / split;
-    r.f = j - r.rem * split;
-    tile = full_tiles + r.rem;
-    r.kb0 = (r.f * kblocks) / split;
-    r.kb1 = ((r.f + 1) * kblocks) / split;
+    // whole tiles (the grid is a multiple of them), then this CTA's share
+    // [c0, c1) of the tail's block run: one or two tile segments
+    const int whole = s.full_tiles / g;
+    if (j < whole) {
+      tile = b + j * g;
+      r.kb0 = 0;
+      r.kb1 = kblocks;
+      r.rem = -1;
+    } else {
+      if (b >= s.chunks) return false;
+      const int run = s.tail_tiles * kblocks;
+      const int c0 = (b * run) / s.chunks, c1 = ((b + 1) * run) / s.chunks;
+      const int t = c0 / kblocks + (j - whole);
+      if (c1 <= c0 || t > (c1 - 1) / kblocks) return false;
+      r.kb0 = max(c0 - t * kblocks, 0);
+      r.kb1 = min(c1 - t * kblocks, kblocks);
+      // shares touching tile t: owner(v), the last share starting at or
+      // before block v, of the tile's first and last blocks
+      const int p0 = ((t * kblocks + 1) * s.chunks - 1) / run;
+      const int p1 = (((t + 1) * kblocks) * s.chunks - 1) / run;
+      tile = s.full_tiles + t;
+      if (p0 == p1) {
+        r.rem = -1;  // the share covers the whole tile
+      } else {
+        r.rem = t;
+        r.slot = t + b;  // unique: shares and tiles both advance monotonically
+        r.base_slot = t + p0;
+        r.nparts = p1 - p0 + 1;
+      }
+    }
   }
   tile_coords(tile, num_m, num_n, r.mt, r.nt);
-  return r;
+  return true;
 }
 
 // Sums SPLIT partial tiles in split order (a fixed order, so results do not
@@ -218,9 +262,9 @@ template <int TILE_M, int GROUP, bool FP32_OUT>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap act_map,
                    const uint8_t* __restrict__ tiles, const __half* __restrict__ scales,
-                   void* __restrict__ c_out, int M, int N, int K, int full_tiles, int split,
-                   int items, uint32_t* __restrict__ tickets, float* __restrict__ partials,
-                   int* status, unsigned long long wait_limit_ns) {
+                   void* __restrict__ c_out, int M, int N, int K, const Sched sched,
+                   uint32_t* __restrict__ tickets, float* __restrict__ partials, int* status,
+                   unsigned long long wait_limit_ns) {
   using L = Cfg<TILE_M>;
   constexpr int A_STAGES = L::A_STAGES;
   constexpr int ACC = L::ACC;
@@ -297,8 +341,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       int last_issue[A_STAGES];
       for (int s = 0; s < A_STAGES; ++s) last_issue[s] = -1;
       bool ok = true;
-      for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
-        const Item w = item_info(item, full_tiles, split, kblocks, num_m, num_n);
+      Item w;
+      for (int j = 0; ok && next_item(sched, blockIdx.x, gridDim.x, j, kblocks, num_m, num_n, w);
+           ++j) {
         const int mt = w.mt;
         for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
           const int s = it % A_STAGES;
@@ -327,8 +372,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       int last_issue[W_STAGES];
       for (int s = 0; s < W_STAGES; ++s) last_issue[s] = -1;
       bool ok = true;
-      for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
-        const Item w = item_info(item, full_tiles, split, kblocks, num_m, num_n);
+      Item w;
+      for (int j = 0; ok && next_item(sched, blockIdx.x, gridDim.x, j, kblocks, num_m, num_n, w);
+           ++j) {
         const uint8_t* wblk = tiles + static_cast<size_t>(w.nt) * kblocks * WBLOCK_BYTES;
         const __half* sblk = scales + static_cast<size_t>(w.nt) * groups * TILE_N;
         for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
@@ -364,8 +410,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       constexpr uint32_t IDESC = idesc_f16_f32(TILE_N, TILE_M);
       uint32_t it = 0, t_local = 0;
       bool ok = true;
-      for (int item = blockIdx.x; item < items && ok; item += gridDim.x, ++t_local) {
-        const Item w = item_info(item, full_tiles, split, kblocks, num_m, num_n);
+      Item w;
+      for (int j = 0; ok && next_item(sched, blockIdx.x, gridDim.x, j, kblocks, num_m, num_n, w);
+           ++j, ++t_local) {
         const int acc = t_local % ACC;
         const uint32_t dph = (t_local / ACC) & 1u;
         if (!mbar_wait(dempty(acc), dph ^ 1u, abort_flag, status, wait_limit_ns)) {
@@ -411,8 +458,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     uint32_t it = static_cast<uint32_t>(dgroup);
     uint32_t total = 0;  // 64-k blocks this CTA processes, over all its items
-    for (int item = blockIdx.x; item < items; item += gridDim.x) {
-      const Item w = item_info(item, full_tiles, split, kblocks, num_m, num_n);
+    Item w;
+    for (int j = 0; next_item(sched, blockIdx.x, gridDim.x, j, kblocks, num_m, num_n, w); ++j) {
       total += static_cast<uint32_t>(w.kb1 - w.kb0);
     }
     for (; it < total; it += DEQ_GROUPS) {
@@ -471,8 +518,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     constexpr int EPI_THREADS = NUM_EPI_WARPS * 32;
     uint32_t t_local = 0;
     bool failed = false;
-    for (int item = blockIdx.x; item < items; item += gridDim.x, ++t_local) {
-      const Item w = item_info(item, full_tiles, split, kblocks, num_m, num_n);
+    Item w;
+    for (int j = 0; next_item(sched, blockIdx.x, gridDim.x, j, kblocks, num_m, num_n, w);
+         ++j, ++t_local) {
       const int acc = t_local % ACC;
       const uint32_t dph = (t_local / ACC) & 1u;
       const bool ok = !failed && mbar_wait(dfull(acc), dph, abort_flag, status, wait_limit_ns);
@@ -540,7 +588,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       // tile is stored as float4 quads [m / 4][n][m % 4], so that each warp
       // access is 512 contiguous bytes.
       float4* mine = reinterpret_cast<float4*>(partials) +
-                     static_cast<size_t>(w.rem * split + w.f) * (TILE_M / 4) * TILE_N;
+                     static_cast<size_t>(w.slot) * (TILE_M / 4) * TILE_N;
       if (ok) {
         tc_fence_after();
 #pragma unroll 1
@@ -565,14 +613,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       if (warp == FIRST_EPI_WARP && lane == 0) *ticket_slot = atomicAdd(&tickets[w.rem], 1u);
       epi_bar_sync(EPI_THREADS);
-      const bool last = *ticket_slot == static_cast<uint32_t>(split - 1);
+      const bool last = *ticket_slot == static_cast<uint32_t>(w.nparts - 1);
       if (last) {
         __threadfence();
         const float4* base = reinterpret_cast<const float4*>(partials) +
-                             static_cast<size_t>(w.rem * split) * (TILE_M / 4) * TILE_N +
+                             static_cast<size_t>(w.base_slot) * (TILE_M / 4) * TILE_N +
                              static_cast<size_t>(half * COLS / 4) * TILE_N + row;
         const int mq = w.mt * TILE_M + half * COLS;
-        switch (split) {
+        switch (w.nparts) {
           case 2:
             reduce_partials<TILE_M, 2, 4, FP32_OUT>(base, c_out, mq, n, M, N, COLS / 4);
             break;
@@ -600,34 +648,70 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 // ------------------------------------------------------------------- host
 
-Plan make_plan(int tile_m, int M, int N, int K, int sm_count, bool allow_split) {
+// Tail schedules are compared with a cost model fitted to B200 timings:
+// one tile of `kblocks` blocks takes kblocks * kBlockUs; a tail of equal
+// splits adds kSplitUs (the partial stores, tickets and reduction), a
+// stream-K tail kStreamKUs (two partial items per CTA and up to four partial
+// tiles per output tile).
+constexpr double kBlockUs256 = 0.45, kBlockUs128 = 0.5;
+constexpr double kSplitUs = 12.0, kStreamKUs = 20.0;
+
+Plan make_plan(int tile_m, int M, int N, int K, int sm_count, size_t budget,
+               bool allow_stream_k) {
   Plan p;
   const int tiles = ((M + tile_m - 1) / tile_m) * (N / TILE_N);
-  p.full_tiles = tiles;
-  p.split = 1;
-  p.items = tiles;
+  const int kblocks = K / BK;
+  p.sched = Sched{tiles, 1, tiles, 0, 0};
+  p.grid = tiles < sm_count ? tiles : sm_count;
   p.workspace_bytes = 0;
-  if (!allow_split) return p;
+  if (budget == 0) return p;
   const int waves = tiles / sm_count;
   const int rem = tiles - waves * sm_count;
   if (rem == 0 || rem * 4 > static_cast<int>(kTicketBytes)) return p;
+  const size_t tile_bytes = static_cast<size_t>(tile_m) * TILE_N * 4;
+  const double t_tile = kblocks * (tile_m > 128 ? kBlockUs256 : kBlockUs128);
+  double best = (waves + 1) * t_tile;  // whole tiles
+
+  // equal splits of each tail tile: at most four, each at least eight blocks
   int f = sm_count / rem;
   f = f < 4 ? f : 4;
-  const int kcap = (K / BK) / 8;  // each split keeps at least eight 64-k blocks
-  f = f < kcap ? f : kcap;
-  if (f < 2) return p;
-  p.full_tiles = waves * sm_count;
-  p.split = f;
-  p.items = p.full_tiles + rem * f;
-  p.workspace_bytes = kTicketBytes + static_cast<size_t>(rem) * f * tile_m * TILE_N * 4;
+  f = f < kblocks / 8 ? f : kblocks / 8;
+  const size_t split_bytes = kTicketBytes + static_cast<size_t>(rem) * f * tile_bytes;
+  if (f >= 2 && split_bytes <= budget && (waves + 1.0 / f) * t_tile + kSplitUs < best) {
+    best = (waves + 1.0 / f) * t_tile + kSplitUs;
+    p.sched = Sched{waves * sm_count, f, waves * sm_count + rem * f, 0, 0};
+    p.grid = p.sched.items < sm_count ? p.sched.items : sm_count;
+    p.workspace_bytes = split_bytes;
+  }
+  if (allow_stream_k) {
+    // equal shares of the tail's blocks, one per CTA: at least eight blocks
+    // each, at most four shares per tile, more shares than tiles
+    const long run = static_cast<long>(rem) * kblocks;
+    int chunks = sm_count;
+    chunks = chunks < 3 * rem ? chunks : 3 * rem;
+    chunks = static_cast<long>(chunks) < run / 8 ? chunks : static_cast<int>(run / 8);
+    int most = 0;
+    for (int t = 0; t < rem && chunks > rem; ++t) {
+      const long p0 = ((static_cast<long>(t) * kblocks + 1) * chunks - 1) / run;
+      const long p1 = ((static_cast<long>(t + 1) * kblocks) * chunks - 1) / run;
+      most = static_cast<int>(p1 - p0 + 1) > most ? static_cast<int>(p1 - p0 + 1) : most;
+    }
+    const size_t sk_bytes = kTicketBytes + static_cast<size_t>(rem + chunks - 1) * tile_bytes;
+    const double sk_time = (waves + static_cast<double>(rem) / chunks) * t_tile + kStreamKUs;
+    if (chunks > rem && most <= 4 && run * chunks < (1l << 31) && sk_bytes <= budget &&
+        sk_time < best) {
+      p.sched = Sched{waves * sm_count, 1, 0, chunks, rem};
+      p.grid = waves > 0 ? sm_count : chunks;
+      p.workspace_bytes = sk_bytes;
+    }
+  }
   return p;
 }
 
 template <int TILE_M, int GROUP, bool FP32_OUT>
 cudaError_t launch_impl(const CUtensorMap& act_map, const uint8_t* tiles, const __half* scales,
-                        void* c, int M, int N, int K, int sm_count, const Plan& plan,
-                        void* workspace, int* status, unsigned long long wait_limit_ns,
-                        cudaStream_t stream) {
+                        void* c, int M, int N, int K, const Plan& plan, void* workspace,
+                        int* status, unsigned long long wait_limit_ns, cudaStream_t stream) {
   using L = Cfg<TILE_M>;
   auto kernel = gemm_tc_kernel<TILE_M, GROUP, FP32_OUT>;
   static bool configured = false;  // per instantiation; idempotent attribute
@@ -637,32 +721,32 @@ cudaError_t launch_impl(const CUtensorMap& act_map, const uint8_t* tiles, const 
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  const int grid = plan.items < sm_count ? plan.items : sm_count;
+  const int grid = plan.grid;
   uint32_t* tickets = static_cast<uint32_t*>(workspace);
   float* partials = workspace ? reinterpret_cast<float*>(static_cast<char*>(workspace) +
                                                          kTicketBytes)
                               : nullptr;
   kernel<<<grid, THREADS, L::DYN_BYTES, stream>>>(act_map, tiles, scales, c, M, N, K,
-                                                  plan.full_tiles, plan.split, plan.items,
-                                                  tickets, partials, status, wait_limit_ns);
+                                                  plan.sched, tickets, partials, status,
+                                                  wait_limit_ns);
   return cudaGetLastError();
 }
 
 template <int TILE_M, bool FP32_OUT>
 cudaError_t launch_group(const CUtensorMap& act_map, const uint8_t* tiles,
                          const __half* scales, void* c, int M, int N, int K, int group,
-                         int sm_count, const Plan& plan, void* workspace, int* status,
+                         const Plan& plan, void* workspace, int* status,
                          unsigned long long wait_limit_ns, cudaStream_t stream) {
   switch (group) {
     case 32:
-      return launch_impl<TILE_M, 32, FP32_OUT>(act_map, tiles, scales, c, M, N, K, sm_count,
-                                               plan, workspace, status, wait_limit_ns, stream);
+      return launch_impl<TILE_M, 32, FP32_OUT>(act_map, tiles, scales, c, M, N, K, plan,
+                                               workspace, status, wait_limit_ns, stream);
     case 64:
-      return launch_impl<TILE_M, 64, FP32_OUT>(act_map, tiles, scales, c, M, N, K, sm_count,
-                                               plan, workspace, status, wait_limit_ns, stream);
+      return launch_impl<TILE_M, 64, FP32_OUT>(act_map, tiles, scales, c, M, N, K, plan,
+                                               workspace, status, wait_limit_ns, stream);
     default:
-      return launch_impl<TILE_M, 128, FP32_OUT>(act_map, tiles, scales, c, M, N, K, sm_count,
-                                                plan, workspace, status, wait_limit_ns, stream);
+      return launch_impl<TILE_M, 128, FP32_OUT>(act_map, tiles, scales, c, M, N, K, plan,
+                                               workspace, status, wait_limit_ns, stream);
   }
 }
 
@@ -676,16 +760,14 @@ int choose_tile_m(int M, int N, int sm_count) {
 
 cudaError_t launch(const CUtensorMap& act_map, int tile_m, const uint8_t* tiles,
                    const __half* scales, void* c, bool fp32_out, int M, int N, int K, int group,
-                   int sm_count, const Plan& plan, void* workspace, int* status,
+                   const Plan& plan, void* workspace, int* status,
                    unsigned long long wait_limit_ns, cudaStream_t stream) {
 #define I4G_TC_CASE(TM)                                                                       \
   if (tile_m == TM)                                                                           \
-    return fp32_out ? launch_group<TM, true>(act_map, tiles, scales, c, M, N, K, group,       \
-                                             sm_count, plan, workspace, status,               \
-                                             wait_limit_ns, stream)                           \
+    return fp32_out ? launch_group<TM, true>(act_map, tiles, scales, c, M, N, K, group, plan, \
+                                             workspace, status, wait_limit_ns, stream)        \
                     : launch_group<TM, false>(act_map, tiles, scales, c, M, N, K, group,      \
-                                              sm_count, plan, workspace, status,              \
-                                              wait_limit_ns, stream);
+                                              plan, workspace, status, wait_limit_ns, stream);
   I4G_TC_CASE(128)
   I4G_TC_CASE(256)
 #undef I4G_TC_CASE

@@ -11,19 +11,29 @@ namespace tc {
 // Ticket counters at the start of a split-K workspace, then the FP32 partials.
 constexpr size_t kTicketBytes = 1024;
 
-// Work schedule of one launch: `full_tiles` whole tiles, then the remaining
-// tiles split `split` ways along K (items = full_tiles + rest * split).
+// Work schedule of one launch (device-visible): `full_tiles` whole tiles,
+// then the tail. chunks == 0: each of the following tiles split `split` ways
+// along K (items = full_tiles + tail * split). chunks > 0 (stream-K): the
+// `tail_tiles` tiles' blocks cut into `chunks` equal shares, one per CTA.
+struct Sched {
+  int full_tiles, split, items, chunks, tail_tiles;
+};
+
 struct Plan {
-  int full_tiles, split, items;
+  Sched sched;
+  int grid;
   size_t workspace_bytes;  // 0 when nothing is split
 };
-Plan make_plan(int tile_m, int M, int N, int K, int sm_count, bool allow_split);
+// The schedule for a workspace of `budget` bytes (0: none): stream-K when it
+// fits (and allow_stream_k), else equal splits when they fit, else whole tiles.
+Plan make_plan(int tile_m, int M, int N, int K, int sm_count, size_t budget,
+               bool allow_stream_k);
 
 // TILE_M (activation rows per tile, the MMA-N) for a problem on sm_count SMs.
 int choose_tile_m(int M, int N, int sm_count);
 cudaError_t launch(const CUtensorMap& act_map, int tile_m, const uint8_t* tiles,
                    const __half* scales, void* c, bool fp32_out, int M, int N, int K,
-                   int group, int sm_count, const Plan& plan, void* workspace, int* status,
+                   int group, const Plan& plan, void* workspace, int* status,
                    unsigned long long wait_limit_ns, cudaStream_t stream);
 }  // namespace tc
 

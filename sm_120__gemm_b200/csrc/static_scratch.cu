@@ -12,11 +12,11 @@
 namespace i4g {
 namespace {
 
-// Holds the split-K workspace of every shape on a device with up to 159 SMs:
-// the plan splits at most sm_count partial tiles of 256 x 128 FP32 (128 KiB)
-// plus 1 KiB of arrival counters. Static device storage is zero-initialised
-// when the module loads.
-constexpr size_t kStaticScratchBytes = size_t(20) << 20;
+// Holds the split-K workspace of every shape on a device with up to 160 SMs:
+// a plan stores at most 2 * sm_count - 1 partial tiles of 256 x 128 FP32
+// (128 KiB) plus 1 KiB of arrival counters. Static device storage is
+// zero-initialised when the module loads.
+constexpr size_t kStaticScratchBytes = size_t(40) << 20;
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
 constexpr int kMaxDevices = 64;

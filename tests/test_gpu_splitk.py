@@ -1,9 +1,11 @@
-"""Split-K schedule of the tcgen05 kernel (the *_ws entry points).
+"""Split-K schedules of the tcgen05 kernel (the *_ws entry points).
 
-The tiles of the last, partial wave are split along K and reduced through a
-caller-owned FP32 workspace in a fixed order. Results are checked against the
-oracle under the same tolerance as the unsplit kernel (tests/parity.py), are
-bitwise reproducible, and leave the workspace counters at zero.
+The tiles of the last, partial wave are shared out along K (stream-K shares
+over all SMs, or equal splits when the workspace is smaller) and reduced
+through a caller-owned FP32 workspace in a fixed order. Results are checked
+against the oracle under the same tolerance as the unsplit kernel
+(tests/parity.py), are bitwise reproducible, and leave the workspace counters
+at zero.
 """
 import numpy as np
 import pytest
@@ -27,16 +29,34 @@ def i4g():
     return m
 
 
-def expected_plan(M, N, K):
-    """(split, remainder tiles) the host plans for this shape on cuda:0."""
+def expected_plan(M, N, K, budget=1 << 62):
+    """The schedule the host plans for this shape on cuda:0 (mirrors
+    make_plan and its cost model): (kind, workspace bytes, tile_m) with kind
+    "stream-k", "split<F>" or "whole"."""
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     tile_m = 128 if M <= 128 else 256
     tiles = -(-M // tile_m) * (N // TILE_N)
-    rem = tiles % sms
-    f = min(4, sms // rem if rem else 0, (K // 64) // 8)
-    if rem == 0 or f < 2:
-        return 1, 0, tile_m
-    return f, rem, tile_m
+    kb = K // 64
+    waves, rem = divmod(tiles, sms)
+    tile_bytes = tile_m * TILE_N * 4
+    if rem == 0 or rem * 4 > TICKET_BYTES:
+        return "whole", 0, tile_m
+    t_tile = kb * (0.45 if tile_m > 128 else 0.5)
+    best, plan = (waves + 1) * t_tile, ("whole", 0, tile_m)
+    f = min(4, sms // rem, kb // 8)
+    need = TICKET_BYTES + rem * f * tile_bytes
+    if f >= 2 and need <= budget and (waves + 1.0 / f) * t_tile + 12.0 < best:
+        best, plan = (waves + 1.0 / f) * t_tile + 12.0, (f"split{f}", need, tile_m)
+    run = rem * kb
+    chunks = min(sms, 3 * rem, run // 8)
+    if chunks > rem:
+        most = max((((t + 1) * kb) * chunks - 1) // run - ((t * kb + 1) * chunks - 1) // run + 1
+                   for t in range(rem))
+        need = TICKET_BYTES + (rem + chunks - 1) * tile_bytes
+        t_sk = (waves + rem / chunks) * t_tile + 20.0
+        if most <= 4 and run * chunks < 2**31 and need <= budget and t_sk < best:
+            plan = ("stream-k", need, tile_m)
+    return plan
 
 
 def fresh_workspace(i4g, M, N, K):
@@ -45,11 +65,11 @@ def fresh_workspace(i4g, M, N, K):
 
 
 @pytest.mark.parametrize("M,N,K", [(4096, 4096, 4096), (512, 1024, 4096), (300, 640, 2048),
-                                   (16, 4096, 4096), (4096, 4096, 448), (2048, 9472, 1024)])
+                                   (16, 4096, 4096), (4096, 4096, 448), (2048, 9472, 1024),
+                                   (1024, 7168, 8192), (2048, 640, 8192)])
 def test_workspace_size(i4g, M, N, K):
-    f, rem, tile_m = expected_plan(M, N, K)
-    want = 0 if (f == 1 or M <= 16) else TICKET_BYTES + rem * f * tile_m * TILE_N * 4
-    assert i4g.gemm_workspace_size(M, N, K) == want
+    kind, need, _ = expected_plan(M, N, K)
+    assert i4g.gemm_workspace_size(M, N, K) == (0 if M <= 16 else need), kind
 
 
 def split_case(i4g, M, N, K, grp, rows=None, fp32_out=False, seed=0):
@@ -76,13 +96,20 @@ def split_case(i4g, M, N, K, grp, rows=None, fp32_out=False, seed=0):
     return rep, c, (a.cuda(), lin, ws)
 
 
-@pytest.mark.parametrize("M,N,K,grp", [(512, 1024, 4096, 128), (300, 640, 2048, 32),
-                                       (1000, 1280, 1024, 64), (130, 384, 1536, 64),
-                                       (2048, 9600, 1024, 32)])
-def test_split_parity(i4g, M, N, K, grp):
-    assert expected_plan(M, N, K)[0] > 1, "shape chosen to exercise the split"
-    rep, _, _ = split_case(i4g, M, N, K, grp)
-    print("split", M, N, K, grp, rep)
+def sample_rows(M, seed):
+    rng = np.random.default_rng(seed)
+    return np.unique(np.concatenate([np.arange(0, 4), np.arange(M // 2 - 2, M // 2 + 2),
+                                     np.arange(M - 4, M), rng.choice(M, 8, replace=False)]))
+
+
+@pytest.mark.parametrize("M,N,K,grp,kind", [(512, 1024, 4096, 128, "split4"),
+                                            (128, 7168, 8192, 64, "split2"),
+                                            (2048, 640, 8192, 32, "split3"),
+                                            (4096, 4864, 4096, 64, "split4")])
+def test_split_parity(i4g, M, N, K, grp, kind):
+    assert expected_plan(M, N, K)[0] == kind, "shape chosen to exercise this schedule"
+    rep, _, _ = split_case(i4g, M, N, K, grp, rows=sample_rows(M, M + N))
+    print(kind, M, N, K, grp, rep)
     assert rep["ok"], rep
 
 
@@ -99,9 +126,10 @@ def test_split_4096_sampled_rows(i4g, grp):
     assert rep["ok"], rep
 
 
-@pytest.mark.parametrize("M,N,K,grp", [(512, 1024, 4096, 64), (300, 640, 2048, 128)])
+@pytest.mark.parametrize("M,N,K,grp", [(512, 1024, 4096, 64), (2048, 640, 8192, 128)])
 def test_split_fp32_output(i4g, M, N, K, grp):
-    rep, _, _ = split_case(i4g, M, N, K, grp, fp32_out=True)
+    assert expected_plan(M, N, K)[0] != "whole"
+    rep, _, _ = split_case(i4g, M, N, K, grp, fp32_out=True, rows=sample_rows(M, 7))
     print("split fp32", M, N, K, grp, rep)
     assert rep["ok"], rep
 
@@ -110,11 +138,11 @@ def test_split_reuse_is_bitwise_reproducible(i4g):
     """One workspace across launches of different shapes: every launch
     returns the counters to zero, so repeated results are bitwise equal."""
     _, c_a, (a_a, lin_a, _) = split_case(i4g, 512, 1024, 4096, 128, rows=np.arange(2))
-    _, c_b, (a_b, lin_b, _) = split_case(i4g, 1000, 1280, 1024, 64, rows=np.arange(2), seed=1)
-    need = max(i4g.gemm_workspace_size(512, 1024, 4096), i4g.gemm_workspace_size(1000, 1280, 1024))
+    _, c_b, (a_b, lin_b, _) = split_case(i4g, 1024, 7168, 8192, 64, rows=np.arange(2), seed=1)
+    need = max(i4g.gemm_workspace_size(512, 1024, 4096), i4g.gemm_workspace_size(1024, 7168, 8192))
     ws = torch.zeros(need, dtype=torch.uint8, device="cuda")
     for _ in range(3):
-        for (a, lin, ref, M) in ((a_a, lin_a, c_a, 512), (a_b, lin_b, c_b, 1000)):
+        for (a, lin, ref, M) in ((a_a, lin_a, c_a, 512), (a_b, lin_b, c_b, 1024)):
             c = torch.empty_like(ref)
             i4g.launch_final_ws(a, lin.tiles, lin.scales, c, M, lin.N, lin.K, lin.group, ws)
             torch.cuda.synchronize()
@@ -150,3 +178,42 @@ def test_misaligned_workspace_rejected(i4g):
     with pytest.raises(i4g.I4GError) as e:
         i4g.launch_final_ws(a, tiles, scales, c, M, N, K, 128, ws[16:])
     assert e.value.status == -4
+
+
+@pytest.mark.parametrize("M,N,K,grp", [(1024, 7168, 8192, 64), (2048, 3968, 12288, 32),
+                                       (1024, 3200, 12288, 128)])
+def test_stream_k_tail_parity(i4g, M, N, K, grp):
+    """Stream-K shares over all SMs (after whole waves, or as the only wave),
+    up to three or four partial tiles per output tile; sampled rows cover the
+    tail tiles' row blocks."""
+    assert expected_plan(M, N, K)[0] == "stream-k"
+    rep, c, (a, lin, ws) = split_case(i4g, M, N, K, grp, rows=sample_rows(M, K))
+    print("stream-k", M, N, K, grp, rep)
+    assert rep["ok"], rep
+    c2 = torch.empty_like(c)
+    i4g.launch_final_ws(a, lin.tiles, lin.scales, c2, M, N, K, grp, ws)
+    torch.cuda.synchronize()
+    assert torch.equal(c.view(torch.int16), c2.view(torch.int16))
+
+
+def test_smaller_workspace_falls_back_to_equal_splits(i4g):
+    """4096^3 with a 20 MiB workspace: the equal two-way split; it must match
+    the oracle."""
+    M = N = K = 4096
+    kind, need, _ = expected_plan(M, N, K, budget=20 << 20)
+    assert kind == "split2"
+    a, w = make_inputs(M, N, K, seed_a=5, seed_b=6)
+    lin = i4g.QuantizedLinear.from_weight(w.cuda(), 128)
+    ws = torch.zeros(20 << 20, dtype=torch.uint8, device="cuda")
+    c = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    i4g.launch_final_ws(a.cuda(), lin.tiles, lin.scales, c, M, N, K, 128, ws)
+    torch.cuda.synchronize()
+    assert i4g.device_status() == 0
+    assert int(ws[:TICKET_BYTES].count_nonzero()) == 0
+    a16 = u16(a)
+    packed, scales = oracle.quantize(u16(w), K, N, 128)
+    deq = oracle.dequantize(packed, scales, K, N, 128)
+    rows = np.array([0, 1, 2047, 3000, 4095])
+    rep = gemm_report(u16(c)[rows], oracle.gemm_rows(a16, deq, M, N, K, rows=rows, threads=8),
+                      oracle.abs_gemm_rows(a16, deq, M, N, K, rows=rows), K)
+    assert rep["ok"], rep

@@ -35,7 +35,8 @@ def test_static_scratch_rejects_bad_shapes_without_a_gpu():
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("M,N,K,grp", [(4096, 4096, 4096, 128), (512, 1024, 4096, 64),
-                                       (300, 640, 2048, 32), (8, 4096, 4096, 128)])
+                                       (1024, 7168, 8192, 64), (300, 640, 2048, 32),
+                                       (8, 4096, 4096, 128)])
 def test_static_scratch_matches_workspace_entry_point(M, N, K, grp):
     if not torch.cuda.is_available():
         pytest.skip("needs a GPU")
