@@ -10,6 +10,9 @@ or shipped. It binds two shared libraries with ctypes:
 * ``_ref/libi4g_ref.so``: ``ref_shim.cu`` compiled together with the
   reference's unmodified ``src/reference.cu`` (built only where the reference
   checkout exists; optional elsewhere).
+* ``_ref/libi4g_refquant.so``: the reference's own GPU quantizer
+  (``src/quantize.cu``) with its fast-math build flag, to measure where it
+  departs from ``quantize_cpu`` (device pointers; needs a GPU to run).
 
 Half-precision arrays travel as ``numpy.uint16`` bit patterns.
 """
@@ -116,6 +119,25 @@ def ref_lib():
             R.i4r_repack_scales_128.argtypes = [_u16p, _u16p, _i, _i, _i]
             _ref = R
     return _ref
+
+
+_REFQ_LIB = os.path.join(HERE, "_ref", "libi4g_refquant.so")
+_refq = None
+
+
+def ref_gpu_quantizer():
+    """The reference's GPU launch_quantize (fast-math build), as
+    i4r_gpu_quantize(b, packed, scales, K, N, group, stream) on device
+    pointers; None when it was not built."""
+    global _refq
+    with _lock:
+        if _refq is None and os.path.exists(_REFQ_LIB):
+            R = ctypes.CDLL(_REFQ_LIB)
+            R.i4r_gpu_quantize.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                           _i, _i, _i, ctypes.c_void_p]
+            R.i4r_gpu_quantize.restype = _i
+            _refq = R
+    return _refq
 
 
 def _p(arr, ptype):
