@@ -85,6 +85,23 @@ inline void launch_quantize_repack(const half* b, uint8_t* tiles, half* repacked
                "launch_quantize_repack");
 }
 
+// New: launch_final / launch_final_fp32 with a split-K workspace (zeroed
+// once; size from i4g_gemm_workspace_size), for shapes whose last wave of
+// output tiles is partial.
+inline void launch_final_ws(const half* a, const uint8_t* b, const half* s, half* c, int M,
+                            int N, int K, int group, void* workspace, size_t workspace_bytes,
+                            cudaStream_t stream) {
+  i4g_throw_if(i4g_gemm_ws(a, b, s, c, M, N, K, group, workspace, workspace_bytes, stream),
+               "launch_final_ws");
+}
+inline void launch_final_fp32_ws(const half* a, const uint8_t* b, const half* s, float* c, int M,
+                                 int N, int K, int group, void* workspace,
+                                 size_t workspace_bytes, cudaStream_t stream) {
+  i4g_throw_if(
+      i4g_gemm_fp32_ws(a, b, s, c, M, N, K, group, workspace, workspace_bytes, stream),
+      "launch_final_fp32_ws");
+}
+
 inline void launch_final(const half* a, const uint8_t* b, const half* s, half* c, int M, int N,
                          int K, int group, cudaStream_t stream) {
   i4g_throw_if(i4g_gemm(a, b, s, c, M, N, K, group, stream), "launch_final");
