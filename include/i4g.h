@@ -185,6 +185,31 @@ int i4g_gemm_static_scratch(const void* A, const uint8_t* tiles,
                             const void* scales, void* C, int M, int N, int K,
                             int group, void* stream);
 
+/* ---- GEMM with the all-gather fused in (no counterpart in the reference) -- */
+
+/* Column-parallel GEMM that writes its column block straight into every
+ * rank's full C: dsts[0..ndst) are the base pointers of ndst row-major
+ * [M][ldc] FP16 matrices (this GPU's and, through pointers from
+ * i4g_ipc_open, its peers'); the launch computes C[:, col0 : col0 + N] =
+ * A x dequant(B) for its slice (tiles, scales: as for i4g_gemm, e.g. a
+ * rank's i4g_shard_range slice) and stores it into all of them over NVLink,
+ * so no separate all-gather runs. 1 <= ndst <= 8. The caller orders the
+ * readers of C after every rank's launch (a cross-rank barrier on the
+ * stream). workspace: as for i4g_gemm_ws (may be NULL). */
+int i4g_gemm_to_peers(const void* A, const uint8_t* tiles, const void* scales,
+                      void* const* dsts, int ndst, int ldc, int col0, int M, int N,
+                      int K, int group, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
+/* Peer mapping of device memory between processes (CUDA IPC; plain
+ * peer-to-peer mappings, no multicast). i4g_ipc_handle: a 64-byte handle of
+ * the allocation holding `ptr` and ptr's byte offset in it. i4g_ipc_open: map
+ * a peer's handle into this process (*base; add the peer's offset).
+ * i4g_ipc_close: unmap. */
+int i4g_ipc_handle(const void* ptr, void* handle, size_t* offset);
+int i4g_ipc_open(const void* handle, void** base);
+int i4g_ipc_close(void* base);
+
 /* ---- column-parallel sharding --------------------------------------------- */
 
 /* Byte offsets of rank `rank`'s slice of a G-way column-parallel split of the

@@ -65,6 +65,11 @@ _SIGNATURES = {
     "i4g_gemm_workspace_size": [_i, _i, _i, ctypes.POINTER(ctypes.c_size_t)],
     "i4g_gemm_ws": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, ctypes.c_size_t, _vp],
     "i4g_gemm_fp32_ws": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, ctypes.c_size_t, _vp],
+    "i4g_gemm_to_peers": [_vp, _vp, _vp, ctypes.POINTER(_vp), _i, _i, _i, _i, _i, _i, _i, _vp,
+                          ctypes.c_size_t, _vp],
+    "i4g_ipc_handle": [_vp, _vp, ctypes.POINTER(ctypes.c_size_t)],
+    "i4g_ipc_open": [_vp, ctypes.POINTER(_vp)],
+    "i4g_ipc_close": [_vp],
     "i4g_shard_range": [_i, _i, _i, _i, _i, ctypes.POINTER(ctypes.c_size_t),
                         ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(_i),
                         ctypes.POINTER(_i)],
@@ -248,6 +253,37 @@ def workspace_for(M: int, N: int, K: int, device=None, stream=None):
         ws = torch.zeros(need, dtype=torch.uint8, device=dev)
         _workspaces[key] = ws
     return ws
+
+
+def launch_final_to_peers(a, b_repacked, scales_repacked, dsts, ldc: int, col0: int, M: int,
+                          N: int, K: int, group: int, workspace=None, stream=None) -> None:
+    """C ABI i4g_gemm_to_peers: this launch's columns [col0, col0 + N) of
+    C = A x dequant(B), written into every matrix of `dsts` (device base
+    pointers of row-major [M][ldc] FP16 matrices, this GPU's and peers')."""
+    arr = (_vp * len(dsts))(*dsts)
+    _call("i4g_gemm_to_peers", _ptr(a), _ptr(b_repacked), _ptr(scales_repacked), arr, len(dsts),
+          ldc, col0, M, N, K, group, _ptr(workspace), 0 if workspace is None else workspace.numel(),
+          _stream(stream))
+
+
+def ipc_handle(t) -> tuple[bytes, int]:
+    """(64-byte CUDA IPC handle of the allocation holding tensor `t`, byte
+    offset of t in it)."""
+    h = ctypes.create_string_buffer(64)
+    off = ctypes.c_size_t()
+    _call("i4g_ipc_handle", _ptr(t), h, ctypes.byref(off))
+    return h.raw, off.value
+
+
+def ipc_open(handle: bytes) -> int:
+    """Map a peer's allocation (from ipc_handle) into this process; base pointer."""
+    base = _vp()
+    _call("i4g_ipc_open", ctypes.create_string_buffer(handle, 64), ctypes.byref(base))
+    return base.value
+
+
+def ipc_close(base: int) -> None:
+    _call("i4g_ipc_close", base)
 
 
 def shard_range(K: int, N: int, group: int, world: int, rank: int):

@@ -392,7 +392,7 @@ def gather_sweep(iters):
 
     import torch.distributed as dist
 
-    from .sharded import ColumnParallelLinear, gather_columns
+    from .sharded import ColumnParallelLinear, PeerOutputs, gather_columns
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -409,7 +409,8 @@ def gather_sweep(iters):
         cp = ColumnParallelLinear(QuantizedLinear.from_weight(w, g), world, rank)
         del w
         if rank == 0:
-            print("M,world,kernel,gemm_us,gemm_plus_gather_us,gather_share")
+            print("M,world,kernel,gemm_us,gemm_plus_nccl_gather_us,fused_peer_store_us,"
+                  "nccl_gather_share")
         for M in (1, 16, 128, 1024, 4096, 16384):
             a = (torch.rand(M, K, generator=gen, device=dev) * 2 - 1).half()
             c_local = torch.empty(M, n_local, dtype=torch.float16, device=dev)
@@ -424,8 +425,16 @@ def gather_sweep(iters):
                 if world > 1:
                     gather_columns(c_local, out=out, gathered=gathered)
 
+            outs = PeerOutputs(M, N, dev) if world > 1 else None
+
+            def fused():
+                if outs is not None:
+                    cp.forward_to_peers(a, outs)
+                else:
+                    cp.forward_local(a, out=c_local)
+
             res = []
-            for fn in (gemm, e2e):
+            for fn in (gemm, e2e, fused):
                 for _ in range(3):
                     fn()
                 torch.cuda.synchronize()
@@ -439,11 +448,13 @@ def gather_sweep(iters):
                 t = torch.tensor([b.elapsed_time(e) * 1e3 / iters], device=dev)
                 dist.all_reduce(t, op=dist.ReduceOp.MAX)
                 res.append(float(t.item()))
+            if outs is not None:
+                outs.close()
             if rank == 0:
                 kern = "decode" if M <= 16 else "tcgen05"
-                print(f"{M},{world},{kern},{res[0]:.2f},{res[1]:.2f},"
+                print(f"{M},{world},{kern},{res[0]:.2f},{res[1]:.2f},{res[2]:.2f},"
                       f"{(res[1] - res[0]) / res[1]:.3f}", flush=True)
-            del a, c_local, gathered, out
+            del a, c_local, gathered, out, outs
             torch.cuda.empty_cache()
         dist.barrier()
     finally:

@@ -194,6 +194,8 @@ int act_map(const void* A, int M, int K, int rows, const CUtensorMap** out) {
 
 unsigned long long g_wait_limit_ns = kDefaultWaitLimitNs;
 
+using MemRangeFn = int (*)(unsigned long long*, size_t*, unsigned long long);
+
 // Tuning override for the tcgen05 kernel's activation tile (128 or 256
 // rows), read once from I4G_TILE_M; 0 means the shape-based choice.
 int tile_m_override() {
@@ -218,18 +220,37 @@ int tc_tile_m(int M, int N, const DeviceInfo* dev) {
   return tile_m_override() ? tile_m_override() : i4g::tc::choose_tile_m(M, N, dev->sm_count);
 }
 
+i4g::Outputs single_output(void* C, int N) {
+  i4g::Outputs o{};
+  o.dst[0] = C;
+  o.count = 1;
+  o.ldc = N;
+  o.col0 = 0;
+  return o;
+}
+
 // `workspace` (nullable) enables the split-K schedule of the tcgen05 kernel
 // when it holds at least the plan's bytes; otherwise the launch is unsplit.
-int gemm_common(const void* A, const uint8_t* tiles, const void* scales, void* C, bool fp32_out,
-                int M, int N, int K, int group, int variant, void* workspace,
+int gemm_common(const void* A, const uint8_t* tiles, const void* scales, const i4g::Outputs& out,
+                bool fp32_out, int M, int N, int K, int group, int variant, void* workspace,
                 size_t workspace_bytes, void* stream) {
-  if (!A || !tiles || !scales || !C) return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
+  if (!A || !tiles || !scales) return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
+  if (out.count < 1 || out.count > i4g::kMaxOutputs)
+    return fail(I4G_ERR_SHAPE, "between 1 and %d output copies (got %d)", i4g::kMaxOutputs,
+                out.count);
+  for (int d = 0; d < out.count; ++d) {
+    if (!out.dst[d]) return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
+    if (!aligned(out.dst[d], fp32_out ? 4 : 2))
+      return fail(I4G_ERR_ALIGNMENT, "C must be aligned to its element size");
+  }
+  if (out.col0 < 0 || out.ldc < out.col0 + N)
+    return fail(I4G_ERR_SHAPE, "columns [%d, %d) do not fit rows of %d", out.col0, out.col0 + N,
+                out.ldc);
   int st = check_shape(M, N, K);
   if (st != I4G_OK) return st;
   st = check_group(K, group, true);
   if (st != I4G_OK) return st;
-  if (!aligned(A, 16) || !aligned(tiles, 16) || !aligned(scales, 16) ||
-      !aligned(C, fp32_out ? 4 : 2))
+  if (!aligned(A, 16) || !aligned(tiles, 16) || !aligned(scales, 16))
     return fail(I4G_ERR_ALIGNMENT, "A, tiles and scales must be 16-byte aligned");
   if (workspace && !aligned(workspace, 256))
     return fail(I4G_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
@@ -252,8 +273,8 @@ int gemm_common(const void* A, const uint8_t* tiles, const void* scales, void* C
     const CUtensorMap* dmap = nullptr;
     st = act_map(A, M, K, -i4g::dec::rows_for(M), &dmap);
     if (st != I4G_OK) return st;
-    return finish(i4g::dec::launch(*dmap, tiles, sc, static_cast<__half*>(C), M, N, K, group,
-                                   dev->sm_count, dev->status_word, g_wait_limit_ns, s),
+    return finish(i4g::dec::launch(*dmap, tiles, sc, out, M, N, K, group, dev->sm_count,
+                                   dev->status_word, g_wait_limit_ns, s),
                   "decode kernel launch");
   }
   const int tile_m = tc_tile_m(M, N, dev);
@@ -262,7 +283,7 @@ int gemm_common(const void* A, const uint8_t* tiles, const void* scales, void* C
   const CUtensorMap* map = nullptr;
   st = act_map(A, M, K, tile_m, &map);
   if (st != I4G_OK) return st;
-  return finish(i4g::tc::launch(*map, tile_m, tiles, sc, C, fp32_out, M, N, K, group, plan,
+  return finish(i4g::tc::launch(*map, tile_m, tiles, sc, out, fp32_out, M, N, K, group, plan,
                                 plan.workspace_bytes > 0 ? workspace : nullptr,
                                 dev->status_word, g_wait_limit_ns, s),
                 "tcgen05 kernel launch");
@@ -463,19 +484,20 @@ int i4g_inverse_repack_umma(const uint8_t* tiles, uint8_t* packed, int K, int N,
 
 int i4g_gemm(const void* A, const uint8_t* tiles, const void* scales, void* C, int M, int N,
              int K, int group, void* stream) {
-  return gemm_common(A, tiles, scales, C, false, M, N, K, group, I4G_VARIANT_AUTO, nullptr, 0,
-                     stream);
+  return gemm_common(A, tiles, scales, single_output(C, N), false, M, N, K, group,
+                     I4G_VARIANT_AUTO, nullptr, 0, stream);
 }
 
 int i4g_gemm_fp32(const void* A, const uint8_t* tiles, const void* scales, float* C, int M,
                   int N, int K, int group, void* stream) {
-  return gemm_common(A, tiles, scales, C, true, M, N, K, group, I4G_VARIANT_TC, nullptr, 0,
-                     stream);
+  return gemm_common(A, tiles, scales, single_output(C, N), true, M, N, K, group,
+                     I4G_VARIANT_TC, nullptr, 0, stream);
 }
 
 int i4g_gemm_variant(const void* A, const uint8_t* tiles, const void* scales, void* C, int M,
                      int N, int K, int group, int variant, void* stream) {
-  return gemm_common(A, tiles, scales, C, false, M, N, K, group, variant, nullptr, 0, stream);
+  return gemm_common(A, tiles, scales, single_output(C, N), false, M, N, K, group, variant,
+                     nullptr, 0, stream);
 }
 
 int i4g_gemm_workspace_size(int M, int N, int K, size_t* bytes) {
@@ -494,15 +516,15 @@ int i4g_gemm_workspace_size(int M, int N, int K, size_t* bytes) {
 
 int i4g_gemm_ws(const void* A, const uint8_t* tiles, const void* scales, void* C, int M, int N,
                 int K, int group, void* workspace, size_t workspace_bytes, void* stream) {
-  return gemm_common(A, tiles, scales, C, false, M, N, K, group, I4G_VARIANT_AUTO, workspace,
-                     workspace_bytes, stream);
+  return gemm_common(A, tiles, scales, single_output(C, N), false, M, N, K, group,
+                     I4G_VARIANT_AUTO, workspace, workspace_bytes, stream);
 }
 
 int i4g_gemm_fp32_ws(const void* A, const uint8_t* tiles, const void* scales, float* C, int M,
                      int N, int K, int group, void* workspace, size_t workspace_bytes,
                      void* stream) {
-  return gemm_common(A, tiles, scales, C, true, M, N, K, group, I4G_VARIANT_TC, workspace,
-                     workspace_bytes, stream);
+  return gemm_common(A, tiles, scales, single_output(C, N), true, M, N, K, group,
+                     I4G_VARIANT_TC, workspace, workspace_bytes, stream);
 }
 
 int i4g_gemm_static_scratch(const void* A, const uint8_t* tiles, const void* scales, void* C,
@@ -534,8 +556,63 @@ int i4g_gemm_static_scratch(const void* A, const uint8_t* tiles, const void* sca
     e = cudaMemsetAsync(scratch, 0, i4g::tc::kTicketBytes, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return record_cuda(e, "clearing the static scratch counters");
   }
-  return gemm_common(A, tiles, scales, C, false, M, N, K, group, I4G_VARIANT_AUTO, scratch, need,
-                     stream);
+  return gemm_common(A, tiles, scales, single_output(C, N), false, M, N, K, group,
+                     I4G_VARIANT_AUTO, scratch, need, stream);
+}
+
+int i4g_gemm_to_peers(const void* A, const uint8_t* tiles, const void* scales, void* const* dsts,
+                      int ndst, int ldc, int col0, int M, int N, int K, int group,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  if (!dsts) return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
+  if (ndst < 1 || ndst > i4g::kMaxOutputs)
+    return fail(I4G_ERR_SHAPE, "between 1 and %d output copies (got %d)", i4g::kMaxOutputs,
+                ndst);
+  i4g::Outputs out{};
+  for (int d = 0; d < ndst; ++d) out.dst[d] = dsts[d];
+  out.count = ndst;
+  out.ldc = ldc;
+  out.col0 = col0;
+  return gemm_common(A, tiles, scales, out, false, M, N, K, group, I4G_VARIANT_AUTO, workspace,
+                     workspace_bytes, stream);
+}
+
+int i4g_ipc_handle(const void* ptr, void* handle, size_t* offset) {
+  if (!ptr || !handle || !offset) return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
+  static MemRangeFn range = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      range = reinterpret_cast<MemRangeFn>(p);
+  });
+  if (!range) return fail(I4G_ERR_DRIVER, "cuMemGetAddressRange is unavailable");
+  unsigned long long base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<unsigned long long>(ptr)) != 0)
+    return fail(I4G_ERR_DRIVER, "cuMemGetAddressRange failed");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return record_cuda(e, "cudaIpcGetMemHandle");
+  std::memcpy(handle, &h, sizeof(h));
+  *offset = reinterpret_cast<unsigned long long>(ptr) - base;
+  return I4G_OK;
+}
+
+int i4g_ipc_open(const void* handle, void** base) {
+  if (!handle || !base) return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? I4G_OK : record_cuda(e, "cudaIpcOpenMemHandle");
+}
+
+int i4g_ipc_close(void* base) {
+  if (!base) return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
+  cudaError_t e = cudaIpcCloseMemHandle(base);
+  return e == cudaSuccess ? I4G_OK : record_cuda(e, "cudaIpcCloseMemHandle");
 }
 
 int i4g_shard_range(int K, int N, int group, int world, int rank, size_t* tile_offset,

@@ -249,7 +249,7 @@ template <int MT, int GROUP, int STAGES>
 __global__ void __launch_bounds__(THREADS, CTAS_PER_SM)
     decode_kernel(const __grid_constant__ CUtensorMap act_map,
                   const uint8_t* __restrict__ tiles, const __half* __restrict__ scales,
-                  __half* __restrict__ c, int M, int N, int K, int* status,
+                  const __grid_constant__ Outputs out, int M, int N, int K, int* status,
                   unsigned long long wait_limit_ns) {
   using L = Layout<MT, GROUP, STAGES>;
   extern __shared__ uint8_t smem_raw[];
@@ -404,22 +404,26 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM)
     const int col = nt * NCOL + w * 16 + (ln >> 2);
     const int m = mb * 8 + 2 * (ln & 3);
     // fragment k: column col + 8 (k >> 1), row m + (k & 1)
-    __half* c0 = c + static_cast<size_t>(m) * N + col;
-    if (m < M) {
-      c0[0] = __float2half_rn(sum.x);
-      c0[8] = __float2half_rn(sum.z);
-    }
-    if (m + 1 < M) {
-      c0[N] = __float2half_rn(sum.y);
-      c0[N + 8] = __float2half_rn(sum.w);
+    const size_t ldc = static_cast<size_t>(out.ldc);
+    for (int d = 0; d < out.count; ++d) {
+      __half* c0 = static_cast<__half*>(out.dst[d]) + static_cast<size_t>(m) * ldc + out.col0 + col;
+      if (m < M) {
+        c0[0] = __float2half_rn(sum.x);
+        c0[8] = __float2half_rn(sum.z);
+      }
+      if (m + 1 < M) {
+        c0[ldc] = __float2half_rn(sum.y);
+        c0[ldc + 8] = __float2half_rn(sum.w);
+      }
     }
   }
+  if (out.count > 1) __threadfence_system();  // peer copies are read by other GPUs
   cluster_sync();  // every CTA's shared memory stays alive until all have read it
 }
 
 template <int MT, int GROUP>
 cudaError_t launch_typed(const CUtensorMap& act_map, const uint8_t* tiles, const __half* scales,
-                         __half* c, int M, int N, int K, int cluster, int* status,
+                         const Outputs& out, int M, int N, int K, int cluster, int* status,
                          unsigned long long wait_limit_ns, cudaStream_t stream) {
   constexpr int S = stages_for<MT, GROUP>();
   using L = Layout<MT, GROUP, S>;
@@ -443,7 +447,7 @@ cudaError_t launch_typed(const CUtensorMap& act_map, const uint8_t* tiles, const
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, act_map, tiles, scales, c, M, N, K, status,
+  return cudaLaunchKernelEx(&cfg, kernel, act_map, tiles, scales, out, M, N, K, status,
                             wait_limit_ns);
 }
 
@@ -484,17 +488,17 @@ int choose_cluster(int N, int K, int sm_count) {
 
 template <int MT>
 cudaError_t launch_mt(const CUtensorMap& act_map, const uint8_t* tiles, const __half* scales,
-                      __half* c, int M, int N, int K, int group, int cluster, int* status,
+                      const Outputs& out, int M, int N, int K, int group, int cluster, int* status,
                       unsigned long long wait_limit_ns, cudaStream_t stream) {
   switch (group) {
     case 32:
-      return launch_typed<MT, 32>(act_map, tiles, scales, c, M, N, K, cluster, status,
+      return launch_typed<MT, 32>(act_map, tiles, scales, out, M, N, K, cluster, status,
                                   wait_limit_ns, stream);
     case 64:
-      return launch_typed<MT, 64>(act_map, tiles, scales, c, M, N, K, cluster, status,
+      return launch_typed<MT, 64>(act_map, tiles, scales, out, M, N, K, cluster, status,
                                   wait_limit_ns, stream);
     default:
-      return launch_typed<MT, 128>(act_map, tiles, scales, c, M, N, K, cluster, status,
+      return launch_typed<MT, 128>(act_map, tiles, scales, out, M, N, K, cluster, status,
                                    wait_limit_ns, stream);
   }
 }
@@ -508,13 +512,13 @@ bool supported(int M, int K, int group) {
 }
 
 cudaError_t launch(const CUtensorMap& act_map, const uint8_t* tiles, const __half* scales,
-                   __half* c, int M, int N, int K, int group, int sm_count, int* status,
+                   const Outputs& out, int M, int N, int K, int group, int sm_count, int* status,
                    unsigned long long wait_limit_ns, cudaStream_t stream) {
   const int cluster = choose_cluster(N, K, sm_count);
   if (M <= 8)
-    return launch_mt<1>(act_map, tiles, scales, c, M, N, K, group, cluster, status,
+    return launch_mt<1>(act_map, tiles, scales, out, M, N, K, group, cluster, status,
                         wait_limit_ns, stream);
-  return launch_mt<2>(act_map, tiles, scales, c, M, N, K, group, cluster, status, wait_limit_ns,
+  return launch_mt<2>(act_map, tiles, scales, out, M, N, K, group, cluster, status, wait_limit_ns,
                       stream);
 }
 

@@ -174,8 +174,8 @@ static __device__ __noinline__ bool next_item(const Sched& s, int b, int g, int 
 // B quads are loaded for every split before any is summed, to overlap the
 // L2 latency.
 template <int TILE_M, int SPLIT, int B, bool FP32_OUT>
-__device__ __forceinline__ void reduce_partials(const float4* base, void* c_out, int m0, int n,
-                                                int M, int N, int quads) {
+__device__ __forceinline__ void reduce_partials(const float4* base, const Outputs& out, int m0,
+                                                int n, int M, int quads) {
   constexpr size_t kSplitStride = static_cast<size_t>(TILE_M / 4) * TILE_N;
 #pragma unroll 1
   for (int q = 0; q < quads; q += B) {
@@ -200,14 +200,18 @@ __device__ __forceinline__ void reduce_partials(const float4* base, void* c_out,
       for (int i = 0; i < 4; ++i) {
         const int m = m0 + 4 * (q + b) + i;
         if (m < M) {
-          if constexpr (FP32_OUT)
-            static_cast<float*>(c_out)[static_cast<size_t>(m) * N + n] = vals[i];
-          else
-            static_cast<__half*>(c_out)[static_cast<size_t>(m) * N + n] = __float2half_rn(vals[i]);
+          const size_t off = static_cast<size_t>(m) * out.ldc + out.col0 + n;
+          for (int d = 0; d < out.count; ++d) {
+            if constexpr (FP32_OUT)
+              static_cast<float*>(out.dst[d])[off] = vals[i];
+            else
+              static_cast<__half*>(out.dst[d])[off] = __float2half_rn(vals[i]);
+          }
         }
       }
     }
   }
+  if (out.count > 1) __threadfence_system();  // peer copies are read by other GPUs
 }
 
 // Named barrier among the epilogue warps (barrier 1); `bar_and` also ANDs a
@@ -262,7 +266,7 @@ template <int TILE_M, int GROUP, bool FP32_OUT>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap act_map,
                    const uint8_t* __restrict__ tiles, const __half* __restrict__ scales,
-                   void* __restrict__ c_out, int M, int N, int K, const Sched sched,
+                   const __grid_constant__ Outputs out, int M, int N, int K, const Sched sched,
                    uint32_t* __restrict__ tickets, float* __restrict__ partials, int* status,
                    unsigned long long wait_limit_ns) {
   using L = Cfg<TILE_M>;
@@ -536,7 +540,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_fence_after();
         if constexpr (FP32_OUT) {
           // FP32 C: store each 16-column chunk as it is read.
-          float* cp = static_cast<float*>(c_out) + static_cast<size_t>(m0) * N + n;
+          const size_t ldc = static_cast<size_t>(out.ldc);
+          const size_t off = static_cast<size_t>(m0) * ldc + out.col0 + n;
 #pragma unroll 1
           for (int c = 0; c < COLS / 16; ++c) {
             uint32_t v[16];
@@ -546,12 +551,14 @@ __global__ void __launch_bounds__(THREADS, 1)
               tc_fence_before();
               mbar_arrive(dempty(acc));
             }
+            for (int d = 0; d < out.count; ++d) {
+              float* cp = static_cast<float*>(out.dst[d]) + off;
 #pragma unroll
-            for (int j = 0; j < 16; ++j)
-              if (m0 + c * 16 + j < M)
-                cp[static_cast<size_t>(c * 16 + j) * N] = __uint_as_float(v[j]);
+              for (int j = 0; j < 16; ++j)
+                if (m0 + c * 16 + j < M) cp[(c * 16 + j) * ldc] = __uint_as_float(v[j]);
+            }
           }
-        } else {
+        } else if (out.count == 1) {
           uint32_t h[COLS / 2];  // packed halves: h[j] = columns 2j, 2j+1
 #pragma unroll
           for (int c = 0; c < COLS / 16; ++c) {
@@ -562,23 +569,52 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           tc_fence_before();
           mbar_arrive(dempty(acc));
-          __half* cp = static_cast<__half*>(c_out) + static_cast<size_t>(m0) * N + n;
+          const size_t ldc = static_cast<size_t>(out.ldc);
+          __half* cp = static_cast<__half*>(out.dst[0]) + static_cast<size_t>(m0) * ldc +
+                       out.col0 + n;
           const int valid = min(COLS, M - m0);
           if (valid >= COLS) {
 #pragma unroll
             for (int j = 0; j < COLS / 2; ++j) {
               const __half2 hv = *reinterpret_cast<const __half2*>(&h[j]);
-              cp[static_cast<size_t>(2 * j) * N] = __low2half(hv);
-              cp[static_cast<size_t>(2 * j + 1) * N] = __high2half(hv);
+              cp[(2 * j) * ldc] = __low2half(hv);
+              cp[(2 * j + 1) * ldc] = __high2half(hv);
             }
           } else {
 #pragma unroll
             for (int j = 0; j < COLS / 2; ++j) {
               const __half2 hv = *reinterpret_cast<const __half2*>(&h[j]);
-              if (2 * j < valid) cp[static_cast<size_t>(2 * j) * N] = __low2half(hv);
-              if (2 * j + 1 < valid) cp[static_cast<size_t>(2 * j + 1) * N] = __high2half(hv);
+              if (2 * j < valid) cp[(2 * j) * ldc] = __low2half(hv);
+              if (2 * j + 1 < valid) cp[(2 * j + 1) * ldc] = __high2half(hv);
             }
           }
+        } else {
+          // Several copies of C (this GPU's and peers'): store each 16-column
+          // chunk to every copy as it is read.
+          const size_t ldc = static_cast<size_t>(out.ldc);
+          const size_t off = static_cast<size_t>(m0) * ldc + out.col0 + n;
+#pragma unroll 1
+          for (int c = 0; c < COLS / 16; ++c) {
+            uint32_t v[16];
+            tmem_ld_32x32b_x16(col0 + c * 16, v);
+            tmem_ld_wait16(v);
+            if (c == COLS / 16 - 1) {
+              tc_fence_before();
+              mbar_arrive(dempty(acc));
+            }
+            uint32_t hv[8];
+            pack_half2(v, hv, 8);
+            for (int d = 0; d < out.count; ++d) {
+              __half* cp = static_cast<__half*>(out.dst[d]) + off;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const __half2 p2 = *reinterpret_cast<const __half2*>(&hv[j]);
+                if (m0 + c * 16 + 2 * j < M) cp[(c * 16 + 2 * j) * ldc] = __low2half(p2);
+                if (m0 + c * 16 + 2 * j + 1 < M) cp[(c * 16 + 2 * j + 1) * ldc] = __high2half(p2);
+              }
+            }
+          }
+          __threadfence_system();  // peer copies are read by other GPUs
         }
         continue;
       }
@@ -622,13 +658,13 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int mq = w.mt * TILE_M + half * COLS;
         switch (w.nparts) {
           case 2:
-            reduce_partials<TILE_M, 2, 4, FP32_OUT>(base, c_out, mq, n, M, N, COLS / 4);
+            reduce_partials<TILE_M, 2, 4, FP32_OUT>(base, out, mq, n, M, COLS / 4);
             break;
           case 3:
-            reduce_partials<TILE_M, 3, 2, FP32_OUT>(base, c_out, mq, n, M, N, COLS / 4);
+            reduce_partials<TILE_M, 3, 2, FP32_OUT>(base, out, mq, n, M, COLS / 4);
             break;
           default:
-            reduce_partials<TILE_M, 4, 2, FP32_OUT>(base, c_out, mq, n, M, N, COLS / 4);
+            reduce_partials<TILE_M, 4, 2, FP32_OUT>(base, out, mq, n, M, COLS / 4);
             break;
         }
       }
@@ -710,7 +746,7 @@ Plan make_plan(int tile_m, int M, int N, int K, int sm_count, size_t budget,
 
 template <int TILE_M, int GROUP, bool FP32_OUT>
 cudaError_t launch_impl(const CUtensorMap& act_map, const uint8_t* tiles, const __half* scales,
-                        void* c, int M, int N, int K, const Plan& plan, void* workspace,
+                        const Outputs& out, int M, int N, int K, const Plan& plan, void* workspace,
                         int* status, unsigned long long wait_limit_ns, cudaStream_t stream) {
   using L = Cfg<TILE_M>;
   auto kernel = gemm_tc_kernel<TILE_M, GROUP, FP32_OUT>;
@@ -726,7 +762,7 @@ cudaError_t launch_impl(const CUtensorMap& act_map, const uint8_t* tiles, const 
   float* partials = workspace ? reinterpret_cast<float*>(static_cast<char*>(workspace) +
                                                          kTicketBytes)
                               : nullptr;
-  kernel<<<grid, THREADS, L::DYN_BYTES, stream>>>(act_map, tiles, scales, c, M, N, K,
+  kernel<<<grid, THREADS, L::DYN_BYTES, stream>>>(act_map, tiles, scales, out, M, N, K,
                                                   plan.sched, tickets, partials, status,
                                                   wait_limit_ns);
   return cudaGetLastError();
@@ -734,18 +770,18 @@ cudaError_t launch_impl(const CUtensorMap& act_map, const uint8_t* tiles, const 
 
 template <int TILE_M, bool FP32_OUT>
 cudaError_t launch_group(const CUtensorMap& act_map, const uint8_t* tiles,
-                         const __half* scales, void* c, int M, int N, int K, int group,
-                         const Plan& plan, void* workspace, int* status,
+                         const __half* scales, const Outputs& out, int M, int N, int K,
+                         int group, const Plan& plan, void* workspace, int* status,
                          unsigned long long wait_limit_ns, cudaStream_t stream) {
   switch (group) {
     case 32:
-      return launch_impl<TILE_M, 32, FP32_OUT>(act_map, tiles, scales, c, M, N, K, plan,
+      return launch_impl<TILE_M, 32, FP32_OUT>(act_map, tiles, scales, out, M, N, K, plan,
                                                workspace, status, wait_limit_ns, stream);
     case 64:
-      return launch_impl<TILE_M, 64, FP32_OUT>(act_map, tiles, scales, c, M, N, K, plan,
+      return launch_impl<TILE_M, 64, FP32_OUT>(act_map, tiles, scales, out, M, N, K, plan,
                                                workspace, status, wait_limit_ns, stream);
     default:
-      return launch_impl<TILE_M, 128, FP32_OUT>(act_map, tiles, scales, c, M, N, K, plan,
+      return launch_impl<TILE_M, 128, FP32_OUT>(act_map, tiles, scales, out, M, N, K, plan,
                                                workspace, status, wait_limit_ns, stream);
   }
 }
@@ -759,14 +795,14 @@ int choose_tile_m(int M, int N, int sm_count) {
 }
 
 cudaError_t launch(const CUtensorMap& act_map, int tile_m, const uint8_t* tiles,
-                   const __half* scales, void* c, bool fp32_out, int M, int N, int K, int group,
-                   const Plan& plan, void* workspace, int* status,
+                   const __half* scales, const Outputs& out, bool fp32_out, int M, int N, int K,
+                   int group, const Plan& plan, void* workspace, int* status,
                    unsigned long long wait_limit_ns, cudaStream_t stream) {
 #define I4G_TC_CASE(TM)                                                                       \
   if (tile_m == TM)                                                                           \
-    return fp32_out ? launch_group<TM, true>(act_map, tiles, scales, c, M, N, K, group, plan, \
-                                             workspace, status, wait_limit_ns, stream)        \
-                    : launch_group<TM, false>(act_map, tiles, scales, c, M, N, K, group,      \
+    return fp32_out ? launch_group<TM, true>(act_map, tiles, scales, out, M, N, K, group,     \
+                                             plan, workspace, status, wait_limit_ns, stream)  \
+                    : launch_group<TM, false>(act_map, tiles, scales, out, M, N, K, group,    \
                                               plan, workspace, status, wait_limit_ns, stream);
   I4G_TC_CASE(128)
   I4G_TC_CASE(256)

@@ -7,6 +7,19 @@
 #include <cstdint>
 
 namespace i4g {
+
+// Where a launch writes C: `count` copies (this GPU's, then peers' through
+// peer-mapped pointers), each a row-major [M][ldc] matrix of which the launch
+// fills columns [col0, col0 + N). count == 1, ldc == N, col0 == 0 is the plain
+// GEMM.
+constexpr int kMaxOutputs = 8;
+struct Outputs {
+  void* dst[kMaxOutputs];
+  int count;
+  int ldc;
+  int col0;
+};
+
 namespace tc {
 // Ticket counters at the start of a split-K workspace, then the FP32 partials.
 constexpr size_t kTicketBytes = 1024;
@@ -32,7 +45,7 @@ Plan make_plan(int tile_m, int M, int N, int K, int sm_count, size_t budget,
 // TILE_M (activation rows per tile, the MMA-N) for a problem on sm_count SMs.
 int choose_tile_m(int M, int N, int sm_count);
 cudaError_t launch(const CUtensorMap& act_map, int tile_m, const uint8_t* tiles,
-                   const __half* scales, void* c, bool fp32_out, int M, int N, int K,
+                   const __half* scales, const Outputs& out, bool fp32_out, int M, int N, int K,
                    int group, const Plan& plan, void* workspace, int* status,
                    unsigned long long wait_limit_ns, cudaStream_t stream);
 }  // namespace tc
@@ -44,7 +57,7 @@ bool supported(int M, int K, int group);
 // Rows of the activation box the decode kernel's tensor map must use.
 int rows_for(int M);
 cudaError_t launch(const CUtensorMap& act_map, const uint8_t* tiles, const __half* scales,
-                   __half* c, int M, int N, int K, int group, int sm_count, int* status,
+                   const Outputs& out, int M, int N, int K, int group, int sm_count, int* status,
                    unsigned long long wait_limit_ns, cudaStream_t stream);
 }  // namespace dec
 

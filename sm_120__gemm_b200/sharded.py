@@ -16,6 +16,7 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
+from . import ipc_close, ipc_handle, ipc_open, launch_final_to_peers, workspace_for
 from .linear import QuantizedLinear
 
 
@@ -38,6 +39,48 @@ def gather_columns(c_local: torch.Tensor, group=None, out: torch.Tensor | None =
         gathered = torch.empty(world * M * n_local, dtype=c_local.dtype, device=c_local.device)
     dist.all_gather_into_tensor(gathered, c_local.contiguous().view(-1), group=group)
     return assemble_columns(gathered, world, M, n_local, out)
+
+
+class PeerOutputs:
+    """Every rank's full C buffer ([max_m, N] FP16), mapped into every rank
+    (CUDA IPC, plain peer-to-peer mappings), so that one GEMM launch per rank
+    can write its column block into all of them: the all-gather fused into
+    the GEMM epilogue. Collective: every rank of `group` constructs it."""
+
+    def __init__(self, max_m: int, N: int, device, group=None):
+        self.max_m, self.N, self.group = max_m, N, group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.buf = torch.empty(max_m * N, dtype=torch.float16, device=device)
+        mine = ipc_handle(self.buf)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, mine, group=group)
+        self._opened = []
+        peers = []
+        for r in range(self.world):
+            if r == self.rank:
+                continue
+            h, off = handles[r]
+            base = ipc_open(h)
+            self._opened.append(base)
+            peers.append(base + off)
+        # this GPU's copy first, then the peers' (the kernel writes them in order)
+        self.dsts = [self.buf.data_ptr()] + peers
+        self._flag = torch.zeros(1, dtype=torch.float32, device=device)
+
+    def view(self, M: int) -> torch.Tensor:
+        return self.buf[: M * self.N].view(M, self.N)
+
+    def barrier(self) -> None:
+        """Stream-ordered cross-rank barrier: after it, every rank's launch
+        (and its peer stores) has completed."""
+        dist.all_reduce(self._flag, group=self.group)
+
+    def close(self) -> None:
+        torch.cuda.synchronize()
+        for base in self._opened:
+            ipc_close(base)
+        self._opened = []
 
 
 class ColumnParallelLinear:
@@ -63,3 +106,18 @@ class ColumnParallelLinear:
         if not gather or self.world == 1:
             return c_local
         return gather_columns(c_local, self.group)
+
+    def forward_to_peers(self, a: torch.Tensor, outs: PeerOutputs, stream=None) -> torch.Tensor:
+        """The full C on every rank with no separate collective: this rank's
+        GEMM stores its columns into every rank's buffer over NVLink, then a
+        barrier orders the readers. Returns this rank's [M, N] view."""
+        a = a.contiguous()
+        M = a.shape[0]
+        if M > outs.max_m or outs.N != self.N:
+            raise ValueError("PeerOutputs too small for this call")
+        loc = self.local
+        ws = workspace_for(M, loc.N, loc.K, a.device, stream)
+        launch_final_to_peers(a, loc.tiles, loc.scales, outs.dsts, self.N, self.n0, M, loc.N,
+                              loc.K, loc.group, ws, stream)
+        outs.barrier()
+        return outs.view(M)

@@ -42,11 +42,20 @@ def _worker(rank, world, port, q, M, N, K, group):
         full = i4g.QuantizedLinear.from_weight(w, group)
         cp = ColumnParallelLinear.from_full(full)
         c = cp.forward(a, gather=True)
+        # the all-gather fused into the GEMM: peer stores, then a barrier
+        from sm_120__gemm_b200.sharded import PeerOutputs
+        outs = PeerOutputs(M, N, a.device)
+        c2 = cp.forward_to_peers(a, outs).clone()
         torch.cuda.synchronize()
+        ref = full(a)
+        torch.cuda.synchronize()
+        ok = (bool(torch.equal(c.view(torch.int16), ref.view(torch.int16))) and
+              bool(torch.equal(c2.view(torch.int16), ref.view(torch.int16))))
+        outs.close()
+        flags = [None] * world
+        dist.all_gather_object(flags, ok)
         if rank == 0:
-            ref = full(a)
-            torch.cuda.synchronize()
-            q.put(bool(torch.equal(c.view(torch.int16), ref.view(torch.int16))))
+            q.put(all(flags))
         dist.barrier()
     finally:
         dist.destroy_process_group()
