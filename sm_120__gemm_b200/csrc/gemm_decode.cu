@@ -405,15 +405,20 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM)
     const int m = mb * 8 + 2 * (ln & 3);
     // fragment k: column col + 8 (k >> 1), row m + (k & 1)
     const size_t ldc = static_cast<size_t>(out.ldc);
-    for (int d = 0; d < out.count; ++d) {
-      __half* c0 = static_cast<__half*>(out.dst[d]) + static_cast<size_t>(m) * ldc + out.col0 + col;
+    const size_t off = static_cast<size_t>(m) * ldc + out.col0 + col;
+    const __half hx = __float2half_rn(sum.x), hy = __float2half_rn(sum.y);
+    const __half hz = __float2half_rn(sum.z), hw = __float2half_rn(sum.w);
+    const int copies = out.count;
+#pragma unroll 1
+    for (int d = 0; d < copies; ++d) {
+      __half* c0 = static_cast<__half*>(d == 0 ? out.dst[0] : out.dst[d]) + off;
       if (m < M) {
-        c0[0] = __float2half_rn(sum.x);
-        c0[8] = __float2half_rn(sum.z);
+        c0[0] = hx;
+        c0[8] = hz;
       }
       if (m + 1 < M) {
-        c0[ldc] = __float2half_rn(sum.y);
-        c0[ldc + 8] = __float2half_rn(sum.w);
+        c0[ldc] = hy;
+        c0[ldc + 8] = hw;
       }
     }
   }

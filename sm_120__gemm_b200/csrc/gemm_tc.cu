@@ -173,9 +173,9 @@ static __device__ __noinline__ bool next_item(const Sched& s, int b, int g, int 
 // quads of one split are TILE_N float4 apart, splits (TILE_M/4)*TILE_N.
 // B quads are loaded for every split before any is summed, to overlap the
 // L2 latency.
-template <int TILE_M, int SPLIT, int B, bool FP32_OUT>
+template <int TILE_M, int SPLIT, int B, bool FP32_OUT, bool MULTI>
 __device__ __forceinline__ void reduce_partials(const float4* base, const Outputs& out, int m0,
-                                                int n, int M, int quads) {
+                                                int n, int M, int N, int quads) {
   constexpr size_t kSplitStride = static_cast<size_t>(TILE_M / 4) * TILE_N;
 #pragma unroll 1
   for (int q = 0; q < quads; q += B) {
@@ -200,18 +200,22 @@ __device__ __forceinline__ void reduce_partials(const float4* base, const Output
       for (int i = 0; i < 4; ++i) {
         const int m = m0 + 4 * (q + b) + i;
         if (m < M) {
-          const size_t off = static_cast<size_t>(m) * out.ldc + out.col0 + n;
-          for (int d = 0; d < out.count; ++d) {
-            if constexpr (FP32_OUT)
-              static_cast<float*>(out.dst[d])[off] = vals[i];
-            else
-              static_cast<__half*>(out.dst[d])[off] = __float2half_rn(vals[i]);
+          if constexpr (FP32_OUT) {
+            static_cast<float*>(out.dst[0])[static_cast<size_t>(m) * N + n] = vals[i];
+          } else if constexpr (!MULTI) {
+            static_cast<__half*>(out.dst[0])[static_cast<size_t>(m) * N + n] =
+                __float2half_rn(vals[i]);
+          } else {
+            const size_t off = static_cast<size_t>(m) * out.ldc + out.col0 + n;
+            const __half h = __float2half_rn(vals[i]);
+#pragma unroll 1
+            for (int d = 0; d < out.count; ++d) static_cast<__half*>(out.dst[d])[off] = h;
           }
         }
       }
     }
   }
-  if (out.count > 1) __threadfence_system();  // peer copies are read by other GPUs
+  if constexpr (MULTI) __threadfence_system();  // peer copies are read by other GPUs
 }
 
 // Named barrier among the epilogue warps (barrier 1); `bar_and` also ANDs a
@@ -262,7 +266,14 @@ __device__ __forceinline__ void tmem_ld_wait16(uint32_t (&r)[16]) {
                : "memory");
 }
 
-template <int TILE_M, int GROUP, bool FP32_OUT>
+// OUT selects the C epilogue at compile time, so the plain kernels carry no
+// code for the general one: half C or float C as one row-major [M][N] matrix
+// (out.dst[0]; ldc == N, col0 == 0), or half C written to columns
+// [col0, col0 + N) of out.count row-major [M][ldc] copies (this GPU's and
+// peers').
+enum OutKind : int { kOutHalf = 0, kOutFloat = 1, kOutHalfCopies = 2 };
+
+template <int TILE_M, int GROUP, int OUT>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap act_map,
                    const uint8_t* __restrict__ tiles, const __half* __restrict__ scales,
@@ -272,6 +283,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   using L = Cfg<TILE_M>;
   constexpr int A_STAGES = L::A_STAGES;
   constexpr int ACC = L::ACC;
+  constexpr bool FP32_OUT = OUT == kOutFloat;
+  constexpr bool MULTI = OUT == kOutHalfCopies;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -540,8 +553,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_fence_after();
         if constexpr (FP32_OUT) {
           // FP32 C: store each 16-column chunk as it is read.
-          const size_t ldc = static_cast<size_t>(out.ldc);
-          const size_t off = static_cast<size_t>(m0) * ldc + out.col0 + n;
+          float* cp = static_cast<float*>(out.dst[0]) + static_cast<size_t>(m0) * N + n;
 #pragma unroll 1
           for (int c = 0; c < COLS / 16; ++c) {
             uint32_t v[16];
@@ -551,14 +563,12 @@ __global__ void __launch_bounds__(THREADS, 1)
               tc_fence_before();
               mbar_arrive(dempty(acc));
             }
-            for (int d = 0; d < out.count; ++d) {
-              float* cp = static_cast<float*>(out.dst[d]) + off;
 #pragma unroll
-              for (int j = 0; j < 16; ++j)
-                if (m0 + c * 16 + j < M) cp[(c * 16 + j) * ldc] = __uint_as_float(v[j]);
-            }
+            for (int j = 0; j < 16; ++j)
+              if (m0 + c * 16 + j < M)
+                cp[static_cast<size_t>(c * 16 + j) * N] = __uint_as_float(v[j]);
           }
-        } else if (out.count == 1) {
+        } else if constexpr (!MULTI) {
           uint32_t h[COLS / 2];  // packed halves: h[j] = columns 2j, 2j+1
 #pragma unroll
           for (int c = 0; c < COLS / 16; ++c) {
@@ -569,23 +579,21 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           tc_fence_before();
           mbar_arrive(dempty(acc));
-          const size_t ldc = static_cast<size_t>(out.ldc);
-          __half* cp = static_cast<__half*>(out.dst[0]) + static_cast<size_t>(m0) * ldc +
-                       out.col0 + n;
+          __half* cp = static_cast<__half*>(out.dst[0]) + static_cast<size_t>(m0) * N + n;
           const int valid = min(COLS, M - m0);
           if (valid >= COLS) {
 #pragma unroll
             for (int j = 0; j < COLS / 2; ++j) {
               const __half2 hv = *reinterpret_cast<const __half2*>(&h[j]);
-              cp[(2 * j) * ldc] = __low2half(hv);
-              cp[(2 * j + 1) * ldc] = __high2half(hv);
+              cp[static_cast<size_t>(2 * j) * N] = __low2half(hv);
+              cp[static_cast<size_t>(2 * j + 1) * N] = __high2half(hv);
             }
           } else {
 #pragma unroll
             for (int j = 0; j < COLS / 2; ++j) {
               const __half2 hv = *reinterpret_cast<const __half2*>(&h[j]);
-              if (2 * j < valid) cp[(2 * j) * ldc] = __low2half(hv);
-              if (2 * j + 1 < valid) cp[(2 * j + 1) * ldc] = __high2half(hv);
+              if (2 * j < valid) cp[static_cast<size_t>(2 * j) * N] = __low2half(hv);
+              if (2 * j + 1 < valid) cp[static_cast<size_t>(2 * j + 1) * N] = __high2half(hv);
             }
           }
         } else {
@@ -604,6 +612,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             uint32_t hv[8];
             pack_half2(v, hv, 8);
+#pragma unroll 1
             for (int d = 0; d < out.count; ++d) {
               __half* cp = static_cast<__half*>(out.dst[d]) + off;
 #pragma unroll
@@ -658,13 +667,13 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int mq = w.mt * TILE_M + half * COLS;
         switch (w.nparts) {
           case 2:
-            reduce_partials<TILE_M, 2, 4, FP32_OUT>(base, out, mq, n, M, COLS / 4);
+            reduce_partials<TILE_M, 2, 4, FP32_OUT, MULTI>(base, out, mq, n, M, N, COLS / 4);
             break;
           case 3:
-            reduce_partials<TILE_M, 3, 2, FP32_OUT>(base, out, mq, n, M, COLS / 4);
+            reduce_partials<TILE_M, 3, 2, FP32_OUT, MULTI>(base, out, mq, n, M, N, COLS / 4);
             break;
           default:
-            reduce_partials<TILE_M, 4, 2, FP32_OUT>(base, out, mq, n, M, COLS / 4);
+            reduce_partials<TILE_M, 4, 2, FP32_OUT, MULTI>(base, out, mq, n, M, N, COLS / 4);
             break;
         }
       }
@@ -744,12 +753,12 @@ Plan make_plan(int tile_m, int M, int N, int K, int sm_count, size_t budget,
   return p;
 }
 
-template <int TILE_M, int GROUP, bool FP32_OUT>
+template <int TILE_M, int GROUP, int OUT>
 cudaError_t launch_impl(const CUtensorMap& act_map, const uint8_t* tiles, const __half* scales,
                         const Outputs& out, int M, int N, int K, const Plan& plan, void* workspace,
                         int* status, unsigned long long wait_limit_ns, cudaStream_t stream) {
   using L = Cfg<TILE_M>;
-  auto kernel = gemm_tc_kernel<TILE_M, GROUP, FP32_OUT>;
+  auto kernel = gemm_tc_kernel<TILE_M, GROUP, OUT>;
   static bool configured = false;  // per instantiation; idempotent attribute
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -768,20 +777,20 @@ cudaError_t launch_impl(const CUtensorMap& act_map, const uint8_t* tiles, const 
   return cudaGetLastError();
 }
 
-template <int TILE_M, bool FP32_OUT>
+template <int TILE_M, int OUT>
 cudaError_t launch_group(const CUtensorMap& act_map, const uint8_t* tiles,
                          const __half* scales, const Outputs& out, int M, int N, int K,
                          int group, const Plan& plan, void* workspace, int* status,
                          unsigned long long wait_limit_ns, cudaStream_t stream) {
   switch (group) {
     case 32:
-      return launch_impl<TILE_M, 32, FP32_OUT>(act_map, tiles, scales, out, M, N, K, plan,
+      return launch_impl<TILE_M, 32, OUT>(act_map, tiles, scales, out, M, N, K, plan,
                                                workspace, status, wait_limit_ns, stream);
     case 64:
-      return launch_impl<TILE_M, 64, FP32_OUT>(act_map, tiles, scales, out, M, N, K, plan,
+      return launch_impl<TILE_M, 64, OUT>(act_map, tiles, scales, out, M, N, K, plan,
                                                workspace, status, wait_limit_ns, stream);
     default:
-      return launch_impl<TILE_M, 128, FP32_OUT>(act_map, tiles, scales, out, M, N, K, plan,
+      return launch_impl<TILE_M, 128, OUT>(act_map, tiles, scales, out, M, N, K, plan,
                                                workspace, status, wait_limit_ns, stream);
   }
 }
@@ -798,14 +807,19 @@ cudaError_t launch(const CUtensorMap& act_map, int tile_m, const uint8_t* tiles,
                    const __half* scales, const Outputs& out, bool fp32_out, int M, int N, int K,
                    int group, const Plan& plan, void* workspace, int* status,
                    unsigned long long wait_limit_ns, cudaStream_t stream) {
-#define I4G_TC_CASE(TM)                                                                       \
-  if (tile_m == TM)                                                                           \
-    return fp32_out ? launch_group<TM, true>(act_map, tiles, scales, out, M, N, K, group,     \
-                                             plan, workspace, status, wait_limit_ns, stream)  \
-                    : launch_group<TM, false>(act_map, tiles, scales, out, M, N, K, group,    \
-                                              plan, workspace, status, wait_limit_ns, stream);
-  I4G_TC_CASE(128)
-  I4G_TC_CASE(256)
+  const bool plain = out.count == 1 && out.ldc == N && out.col0 == 0;
+  if (fp32_out && !plain) return cudaErrorInvalidValue;  // float C is one plain matrix
+  const int kind = fp32_out ? kOutFloat : (plain ? kOutHalf : kOutHalfCopies);
+#define I4G_TC_CASE(TM, KIND)                                                              \
+  if (tile_m == TM && kind == KIND)                                                        \
+    return launch_group<TM, KIND>(act_map, tiles, scales, out, M, N, K, group, plan,       \
+                                  workspace, status, wait_limit_ns, stream);
+  I4G_TC_CASE(128, kOutHalf)
+  I4G_TC_CASE(128, kOutFloat)
+  I4G_TC_CASE(128, kOutHalfCopies)
+  I4G_TC_CASE(256, kOutHalf)
+  I4G_TC_CASE(256, kOutFloat)
+  I4G_TC_CASE(256, kOutHalfCopies)
 #undef I4G_TC_CASE
   return cudaErrorInvalidValue;
 }
