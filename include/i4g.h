@@ -148,17 +148,24 @@ int i4g_gemm_variant(const void* A, const uint8_t* tiles, const void* scales,
  * or, with a smaller workspace, each leftover tile split 2 to 4 ways) and
  * reduce the FP32 partial tiles through a caller-owned workspace, in a fixed
  * order, so results are bitwise reproducible and within the usual FP32
- * accumulation tolerance of the unsplit kernel.
+ * accumulation tolerance of the unsplit kernel. The decode kernel (M <= 16,
+ * FP16 C) uses the workspace the same way for its own stream-K schedule:
+ * two CTAs per SM take equal runs of (128-column tile, 64-k block) units, so
+ * every SM does the same work whatever N is, and a tile split between CTAs
+ * is reduced by the last of them to finish, in run order. Without a
+ * workspace it spreads each tile's K over a thread-block cluster instead.
  *
  * i4g_gemm_workspace_size: bytes needed for this shape on the current device
- * (0 when nothing would be split, e.g. M <= 16 or a whole number of waves).
+ * (0 when nothing would be split, e.g. a whole number of waves).
  *
  * i4g_gemm_ws / i4g_gemm_fp32_ws: i4g_gemm / i4g_gemm_fp32 with a workspace.
  * workspace: 256-byte aligned device memory, ZEROED ONCE before its first use
- * (its first 1024 bytes are arrival counters that every launch returns to
+ * (its first 4096 bytes are arrival counters that every launch returns to
  * zero). A workspace smaller than i4g_gemm_workspace_size reports gets the
- * best schedule that fits (equal splits, or whole tiles; NULL: whole tiles). Launches sharing one workspace must be ordered (one
- * stream); concurrent launches on the same workspace race. */
+ * best schedule that fits (equal splits, or whole tiles; NULL: whole tiles;
+ * the decode kernel: its cluster schedule). Launches sharing one workspace
+ * must be ordered (one stream); concurrent launches on the same workspace
+ * race. */
 int i4g_gemm_workspace_size(int M, int N, int K, size_t* bytes);
 int i4g_gemm_ws(const void* A, const uint8_t* tiles, const void* scales, void* C,
                 int M, int N, int K, int group, void* workspace,
@@ -219,6 +226,24 @@ int i4g_ipc_close(void* base);
 int i4g_shard_range(int K, int N, int group, int world, int rank,
                     size_t* tile_offset, size_t* scale_offset,
                     int* n0, int* n1);
+
+/* ---- decode schedule (no counterpart in the reference) --------------------- */
+
+/* The decode kernel (M <= 16, FP16 C) has two schedules: the cluster schedule
+ * (each 128-column tile's K split over a thread-block cluster, reduced
+ * through distributed shared memory; needs no workspace) and the stream-K
+ * schedule of the *_ws entry points (see the workspace section). AUTO (the
+ * default, or the I4G_DECODE_SCHEDULE environment variable's "cluster" /
+ * "streamk" at the first call) picks stream-K when it takes enough work off
+ * the busiest SM to pay for its reduction through global memory; the others
+ * force one (stream-K only where a large enough workspace is given).
+ * Process-wide; affects launches issued after the call. */
+enum {
+  I4G_DECODE_AUTO = 0,
+  I4G_DECODE_CLUSTER = 1,
+  I4G_DECODE_STREAMK = 2
+};
+int i4g_set_decode_schedule(int schedule);
 
 /* ---- device status --------------------------------------------------------- */
 

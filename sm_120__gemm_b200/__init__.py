@@ -75,6 +75,7 @@ _SIGNATURES = {
                         ctypes.POINTER(_i)],
     "i4g_device_status": [ctypes.POINTER(_i), _vp],
     "i4g_selftest_wait_timeout": [ctypes.c_ulonglong, _vp],
+    "i4g_set_decode_schedule": [_i],
     "i4g_layout_version": [],
 }
 
@@ -306,6 +307,15 @@ def device_status(stream=None) -> int:
 
 def selftest_wait_timeout(limit_ns: int, stream=None) -> None:
     _call("i4g_selftest_wait_timeout", limit_ns, _stream(stream))
+
+
+DECODE_SCHEDULES = {"auto": 0, "cluster": 1, "streamk": 2}
+
+
+def set_decode_schedule(schedule: str) -> None:
+    """C ABI i4g_set_decode_schedule: "auto", "cluster" or "streamk", for
+    decode-shaped (M <= 16) launches issued after the call, process-wide."""
+    _call("i4g_set_decode_schedule", DECODE_SCHEDULES[schedule])
 
 
 from .linear import QuantizedLinear  # noqa: E402  (needs the launchers above)

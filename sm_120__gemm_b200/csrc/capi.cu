@@ -274,6 +274,7 @@ int gemm_common(const void* A, const uint8_t* tiles, const void* scales, const i
     st = act_map(A, M, K, -i4g::dec::rows_for(M), &dmap);
     if (st != I4G_OK) return st;
     return finish(i4g::dec::launch(*dmap, tiles, sc, out, M, N, K, group, dev->sm_count,
+                                   workspace, workspace ? workspace_bytes : 0,
                                    dev->status_word, g_wait_limit_ns, s),
                   "decode kernel launch");
   }
@@ -507,10 +508,12 @@ int i4g_gemm_workspace_size(int M, int N, int K, size_t* bytes) {
   if (st != I4G_OK) return st;
   DeviceInfo* dev = nullptr;
   if ((st = current_device(&dev)) != I4G_OK) return st;
-  // the decode kernel needs none (its largest-K limit is for group 32)
-  if (i4g::dec::supported(M, K, 32)) return I4G_OK;
   *bytes = i4g::tc::make_plan(tc_tile_m(M, N, dev), M, N, K, dev->sm_count, SIZE_MAX, true)
                .workspace_bytes;
+  if (i4g::dec::supported(M, K, 32)) {  // FP16 C at these M runs the decode kernel
+    const i4g::dec::SkPlan sk = i4g::dec::sk_plan(M, N, K, dev->sm_count);
+    if (sk.preferred && sk.workspace_bytes > *bytes) *bytes = sk.workspace_bytes;
+  }
   return I4G_OK;
 }
 
@@ -534,9 +537,13 @@ int i4g_gemm_static_scratch(const void* A, const uint8_t* tiles, const void* sca
   DeviceInfo* dev = nullptr;
   if ((st = current_device(&dev)) != I4G_OK) return st;
   size_t need = 0;
-  if (!i4g::dec::supported(M, K, group))
+  if (!i4g::dec::supported(M, K, group)) {
     need = i4g::tc::make_plan(tc_tile_m(M, N, dev), M, N, K, dev->sm_count, SIZE_MAX, true)
                .workspace_bytes;
+  } else {
+    const i4g::dec::SkPlan sk = i4g::dec::sk_plan(M, N, K, dev->sm_count);
+    if (sk.preferred) need = sk.workspace_bytes;
+  }
   if (need > i4g::static_scratch_bytes()) {
     std::snprintf(t_last_error, sizeof(t_last_error),
                   "shape M=%d N=%d K=%d needs %zu bytes of split-K scratch; the static scratch "
@@ -646,6 +653,18 @@ int i4g_device_status(int* out, void* stream) {
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   if (e != cudaSuccess) return record_cuda(e, "reading the device status word");
   *out = value;
+  return I4G_OK;
+}
+
+int i4g_set_decode_schedule(int schedule) {
+  if (schedule != I4G_DECODE_AUTO && schedule != I4G_DECODE_CLUSTER &&
+      schedule != I4G_DECODE_STREAMK)
+    return fail(I4G_ERR_VARIANT, "unknown decode schedule %d", schedule);
+  static_assert(I4G_DECODE_AUTO == i4g::dec::kScheduleAuto &&
+                    I4G_DECODE_CLUSTER == i4g::dec::kScheduleCluster &&
+                    I4G_DECODE_STREAMK == i4g::dec::kScheduleStreamK,
+                "decode schedule codes");
+  i4g::dec::set_schedule(schedule);
   return I4G_OK;
 }
 

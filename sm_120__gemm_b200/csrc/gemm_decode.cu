@@ -29,7 +29,10 @@
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <atomic>
 #include <cstdlib>
+#include <cstring>
 
 namespace i4g {
 namespace dec {
@@ -245,6 +248,104 @@ constexpr int stages_for() {
   return s;
 }
 
+// Producer side of one ring stage: 64-k blocks [kb, kb + nkb) of column
+// tile nt (weights, their scale groups) and the activation box at kb.
+template <int MT, int GROUP, int STAGES>
+__device__ __forceinline__ void issue_stage(const CUtensorMap* act_map, const uint8_t* tiles,
+                                            const __half* scales, int nt, int kb, int nkb,
+                                            int kblocks, int groups, uint32_t dst,
+                                            uint32_t full) {
+  using L = Layout<MT, GROUP, STAGES>;
+  const uint8_t* wsrc = tiles + static_cast<size_t>(nt) * kblocks * 4096;
+  const __half* ssrc = scales + static_cast<size_t>(nt) * groups * 128;
+  const int g0 = kb * BK / GROUP;
+  const int g1 = ((kb + nkb) * BK + GROUP - 1) / GROUP;
+  mbar_arrive_expect_tx(full, L::ABYTES + nkb * 4096 + (g1 - g0) * 256);
+  bulk_load(dst + L::ABYTES, wsrc + static_cast<size_t>(kb) * 4096, nkb * 4096, full);
+  tma_load_3d(dst, act_map, full, 0, 0, kb);
+  bulk_load(dst + L::ABYTES + L::WBYTES, ssrc + static_cast<size_t>(g0) * 128, (g1 - g0) * 256,
+            full);
+}
+
+// Per-lane shared-memory offsets inside a stage (see the fragment mapping at
+// the top of the file).
+struct LaneOffsets {
+  uint32_t w, s, a0, a1;
+};
+
+template <int MT, int GROUP, int STAGES>
+__device__ __forceinline__ LaneOffsets lane_offsets(int warp, int lane) {
+  using L = Layout<MT, GROUP, STAGES>;
+  const int g = lane >> 2, t = lane & 3;
+  const int r0 = warp * 16 + g;  // weight column (inside the tile) of a0/a2
+  LaneOffsets o;
+  o.w = L::ABYTES + (t >> 1) * 2048 + r0 * 16 + (t & 1) * 8;
+  o.s = L::ABYTES + L::WBYTES + r0 * 2;
+  // activation row (mb*8 + g) of block j: box row R = j*ROWS + mb*8 + g, and
+  // R % 8 == g; 16-byte chunks 2t, 2t+1 sit at (chunk ^ g) under the swizzle
+  o.a0 = g * 128 + (((2 * t) ^ g) << 4);
+  o.a1 = g * 128 + (((2 * t + 1) ^ g) << 4);
+  return o;
+}
+
+// Consumer side of one ring stage: nkb 64-k blocks starting at block kb.
+template <int MT, int GROUP, int STAGES>
+__device__ __forceinline__ void compute_stage(uint32_t slot, const LaneOffsets& o, int lane,
+                                              int kb, int nkb, float (&acc)[MT][4][4]) {
+  using L = Layout<MT, GROUP, STAGES>;
+  const int t = lane & 3;
+  const uint32_t wp = slot + o.w;
+  const uint32_t sp = slot + o.s;
+  const uint32_t ap0 = slot + o.a0, ap1 = slot + o.a1;
+  const int odd = kb & 1;
+  if (nkb == KPS) {
+    if constexpr (MT == 1) {
+      block_step2(wp, sp + scale_offset<GROUP>(0, t, odd), sp + scale_offset<GROUP>(1, t, odd),
+                  ap0, ap1, acc);
+      block_step2(wp + 2 * 4096, sp + scale_offset<GROUP>(2, t, odd),
+                  sp + scale_offset<GROUP>(3, t, odd), ap0 + 2 * L::ROWS * 128,
+                  ap1 + 2 * L::ROWS * 128, acc);
+    } else {
+#pragma unroll
+      for (int j = 0; j < KPS; ++j)
+        block_step(wp + j * 4096, sp + scale_offset<GROUP>(j, t, odd),
+                   ap0 + j * (L::ROWS * 128), ap1 + j * (L::ROWS * 128), acc);
+    }
+  } else {
+#pragma unroll 1
+    for (int j = 0; j < nkb; ++j)
+      block_step(wp + j * 4096, sp + scale_offset<GROUP>(j, t, odd), ap0 + j * (L::ROWS * 128),
+                 ap1 + j * (L::ROWS * 128), acc);
+  }
+}
+
+// Writes one lane's four sums of fragment (row block mb) to every copy of C:
+// v.x at (m, col), v.y at (m + 1, col), v.z at (m, col + 8), v.w at
+// (m + 1, col + 8), where col = tile column of the lane (warp w, lane ln)
+// and m = mb * 8 + 2 (ln & 3).
+__device__ __forceinline__ void store_fragment(const Outputs& out, int M, int nt, int w, int ln,
+                                               int mb, float4 v) {
+  const int col = nt * NCOL + w * 16 + (ln >> 2);
+  const int m = mb * 8 + 2 * (ln & 3);
+  const size_t ldc = static_cast<size_t>(out.ldc);
+  const size_t off = static_cast<size_t>(m) * ldc + out.col0 + col;
+  const __half hx = __float2half_rn(v.x), hy = __float2half_rn(v.y);
+  const __half hz = __float2half_rn(v.z), hw = __float2half_rn(v.w);
+  const int copies = out.count;
+#pragma unroll 1
+  for (int d = 0; d < copies; ++d) {
+    __half* c0 = static_cast<__half*>(out.dst[d]) + off;
+    if (m < M) {
+      c0[0] = hx;
+      c0[8] = hz;
+    }
+    if (m + 1 < M) {
+      c0[ldc] = hy;
+      c0[ldc + 8] = hw;
+    }
+  }
+}
+
 template <int MT, int GROUP, int STAGES>
 __global__ void __launch_bounds__(THREADS, CTAS_PER_SM)
     decode_kernel(const __grid_constant__ CUtensorMap act_map,
@@ -286,8 +387,6 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM)
     // --------------------------------------------------------------- producer
     if (lane == 0) {
       prefetch_tensormap(&act_map);
-      const uint8_t* wsrc = tiles + static_cast<size_t>(nt) * kblocks * 4096;
-      const __half* ssrc = scales + static_cast<size_t>(nt) * groups * 128;
       int issued = 0;
       for (int i = 0; i < nstages; ++i) {
         const int s = i % STAGES;
@@ -295,16 +394,8 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM)
         if (!mbar_wait(bars + 8 * (STAGES + s), ph ^ 1u, abort_flag, status, wait_limit_ns)) break;
         issued = i + 1;
         const int kb = kb0 + i * KPS;
-        const int nkb = min(KPS, kb1 - kb);
-        const int g0 = kb * BK / GROUP;
-        const int g1 = ((kb + nkb) * BK + GROUP - 1) / GROUP;
-        const uint32_t dst = ring + s * L::SLOT;
-        const uint32_t full = bars + 8 * s;
-        mbar_arrive_expect_tx(full, L::ABYTES + nkb * 4096 + (g1 - g0) * 256);
-        bulk_load(dst + L::ABYTES, wsrc + static_cast<size_t>(kb) * 4096, nkb * 4096, full);
-        tma_load_3d(dst, &act_map, full, 0, 0, kb);
-        bulk_load(dst + L::ABYTES + L::WBYTES, ssrc + static_cast<size_t>(g0) * 128,
-                  (g1 - g0) * 256, full);
+        issue_stage<MT, GROUP, STAGES>(&act_map, tiles, scales, nt, kb, min(KPS, kb1 - kb),
+                                       kblocks, groups, ring + s * L::SLOT, bars + 8 * s);
       }
       if (issued < nstages) {  // gave up: let the copies already issued land first
         volatile int never = 0;
@@ -314,8 +405,6 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM)
     }
   } else {
     // ---------------------------------------------------------------- compute
-    const int g = lane >> 2, t = lane & 3;
-    const int r0 = warp * 16 + g;  // weight column (inside the tile) of a0/a2
     float acc[MT][4][4];  // [row block][MMA step][fragment]
 #pragma unroll
     for (int mb = 0; mb < MT; ++mb)
@@ -323,42 +412,13 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM)
       for (int q = 0; q < 4; ++q)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[mb][q][i] = 0.0f;
-    const uint32_t wofs = L::ABYTES + (t >> 1) * 2048 + r0 * 16 + (t & 1) * 8;
-    const uint32_t sofs = L::ABYTES + L::WBYTES + r0 * 2;
-    // activation row (mb*8 + g) of block j: box row R = j*ROWS + mb*8 + g, and
-    // R % 8 == g; 16-byte chunks 2t, 2t+1 sit at (chunk ^ g) under the swizzle
-    const uint32_t aofs0 = g * 128 + (((2 * t) ^ g) << 4);
-    const uint32_t aofs1 = g * 128 + (((2 * t + 1) ^ g) << 4);
+    const LaneOffsets o = lane_offsets<MT, GROUP, STAGES>(warp, lane);
     for (int i = 0; i < nstages; ++i) {
       const int s = i % STAGES;
       const uint32_t ph = (i / STAGES) & 1u;
       if (!mbar_wait(bars + 8 * s, ph, abort_flag, status, wait_limit_ns)) break;
-      const uint32_t slot = ring + s * L::SLOT;
       const int kb = kb0 + i * KPS;
-      const int nkb = min(KPS, kb1 - kb);
-      const uint32_t wp = slot + wofs;
-      const uint32_t sp = slot + sofs;
-      const uint32_t ap0 = slot + aofs0, ap1 = slot + aofs1;
-      const int odd = kb & 1;
-      if (nkb == KPS) {
-        if constexpr (MT == 1) {
-          block_step2(wp, sp + scale_offset<GROUP>(0, t, odd), sp + scale_offset<GROUP>(1, t, odd),
-                      ap0, ap1, acc);
-          block_step2(wp + 2 * 4096, sp + scale_offset<GROUP>(2, t, odd),
-                      sp + scale_offset<GROUP>(3, t, odd), ap0 + 2 * L::ROWS * 128,
-                      ap1 + 2 * L::ROWS * 128, acc);
-        } else {
-#pragma unroll
-          for (int j = 0; j < KPS; ++j)
-            block_step(wp + j * 4096, sp + scale_offset<GROUP>(j, t, odd),
-                       ap0 + j * (L::ROWS * 128), ap1 + j * (L::ROWS * 128), acc);
-        }
-      } else {
-#pragma unroll 1
-        for (int j = 0; j < nkb; ++j)
-          block_step(wp + j * 4096, sp + scale_offset<GROUP>(j, t, odd),
-                     ap0 + j * (L::ROWS * 128), ap1 + j * (L::ROWS * 128), acc);
-      }
+      compute_stage<MT, GROUP, STAGES>(ring + s * L::SLOT, o, lane, kb, min(KPS, kb1 - kb), acc);
       __syncwarp();
       if (lane == 0) mbar_arrive(bars + 8 * (STAGES + s));
     }
@@ -398,32 +458,229 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM)
         sum.w += v[r].w;
       }
     }
-    const int mb = x % MT;
     const int th = x / MT;
-    const int w = th >> 5, ln = th & 31;
-    const int col = nt * NCOL + w * 16 + (ln >> 2);
-    const int m = mb * 8 + 2 * (ln & 3);
-    // fragment k: column col + 8 (k >> 1), row m + (k & 1)
-    const size_t ldc = static_cast<size_t>(out.ldc);
-    const size_t off = static_cast<size_t>(m) * ldc + out.col0 + col;
-    const __half hx = __float2half_rn(sum.x), hy = __float2half_rn(sum.y);
-    const __half hz = __float2half_rn(sum.z), hw = __float2half_rn(sum.w);
-    const int copies = out.count;
-#pragma unroll 1
-    for (int d = 0; d < copies; ++d) {
-      __half* c0 = static_cast<__half*>(d == 0 ? out.dst[0] : out.dst[d]) + off;
-      if (m < M) {
-        c0[0] = hx;
-        c0[8] = hz;
-      }
-      if (m + 1 < M) {
-        c0[ldc] = hy;
-        c0[ldc + 8] = hw;
-      }
-    }
+    store_fragment(out, M, nt, th >> 5, th & 31, x % MT, sum);
   }
   if (out.count > 1) __threadfence_system();  // peer copies are read by other GPUs
   cluster_sync();  // every CTA's shared memory stays alive until all have read it
+}
+
+// ---------------------------------------------------------------------------
+// Stream-K schedule. The product has units = (N / 128) * (K / 64) units of
+// one column tile x one 64-k block; a persistent grid of G CTAs (CTAS_PER_SM
+// per SM) gives CTA c the contiguous run [c*units/G, (c+1)*units/G) in
+// tile-major order, so every SM streams and decodes the same number of
+// weights whatever N / 128 is. A run is cut at tile edges into segments. A
+// CTA whose segment covers a whole tile writes that tile of C itself;
+// otherwise it stores its FP32 partial in the workspace, at slot c + tile
+// (unique: each slot index counts the run and tile boundaries before the
+// segment), and the last of the tile's CTAs to arrive (a ticket per tile,
+// indexed by the tile's first CTA, which no other split tile shares) sums
+// the tile's partials in run order, so the result does not depend on
+// arrival order, and writes C.
+
+__host__ __device__ __forceinline__ int sk_owner(long unit, int grid, long units) {
+  // CTA whose run holds `unit`: the largest c with c*units/G <= unit
+  return static_cast<int>(((unit + 1) * grid - 1) / units);
+}
+
+template <int MT>
+constexpr size_t sk_slot_float4s() {
+  return static_cast<size_t>(CWARPS) * 32 * MT;
+}
+
+template <int MT, int GROUP, int STAGES>
+__global__ void __launch_bounds__(THREADS, CTAS_PER_SM)
+    decode_sk_kernel(const __grid_constant__ CUtensorMap act_map,
+                     const uint8_t* __restrict__ tiles, const __half* __restrict__ scales,
+                     const __grid_constant__ Outputs out, int M, int N, int K,
+                     uint32_t* __restrict__ tickets, float4* __restrict__ partials, int* status,
+                     unsigned long long wait_limit_ns) {
+  using L = Layout<MT, GROUP, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const uint32_t ring = smem_u32(smem);
+  const uint32_t bars = ring + L::BARS;  // full[STAGES], empty[STAGES]
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::ABORT);
+  volatile int* last_flag = abort_flag + 1;  // "this CTA reduces the tile", per segment
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int kblocks = K / BK;
+  const int groups = K / GROUP;
+  const long units = static_cast<long>(N / NCOL) * kblocks;
+  const int grid = static_cast<int>(gridDim.x);
+  const int c = static_cast<int>(blockIdx.x);
+  const long u0 = c * units / grid;
+  const long u1 = (c + 1) * units / grid;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(bars + 8 * s, 1);
+      mbar_init(bars + 8 * (STAGES + s), CWARPS);
+    }
+    *abort_flag = 0;
+    fence_mbarrier_init();
+    fence_proxy_async_smem();
+  }
+  __syncthreads();
+
+  if (warp == CWARPS) {
+    // --------------------------------------------------------------- producer
+    if (lane == 0) {
+      prefetch_tensormap(&act_map);
+      int i = 0, issued = 0;
+      bool ok = true;
+      for (long u = u0; ok && u < u1;) {
+        const int nt = static_cast<int>(u / kblocks);
+        const int kb_end = static_cast<int>(min(u1 - static_cast<long>(nt) * kblocks,
+                                                static_cast<long>(kblocks)));
+        for (int kb = static_cast<int>(u - static_cast<long>(nt) * kblocks); kb < kb_end;
+             kb += KPS, ++i) {
+          const int s = i % STAGES;
+          const uint32_t ph = (i / STAGES) & 1u;
+          if (!mbar_wait(bars + 8 * (STAGES + s), ph ^ 1u, abort_flag, status, wait_limit_ns)) {
+            ok = false;
+            break;
+          }
+          issued = i + 1;
+          issue_stage<MT, GROUP, STAGES>(&act_map, tiles, scales, nt, kb, min(KPS, kb_end - kb),
+                                         kblocks, groups, ring + s * L::SLOT, bars + 8 * s);
+        }
+        u = static_cast<long>(nt) * kblocks + kb_end;
+      }
+      if (!ok) {  // gave up: let the copies already issued land first
+        volatile int never = 0;
+        for (int j = (issued > STAGES ? issued - STAGES : 0); j < issued; ++j)
+          mbar_wait(bars + 8 * (j % STAGES), (j / STAGES) & 1u, &never, nullptr, 100000000ull);
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ compute
+  constexpr int CTHREADS = CWARPS * 32;
+  constexpr size_t SLOT4 = sk_slot_float4s<MT>();
+  float acc[MT][4][4];  // [row block][MMA step][fragment]
+#pragma unroll
+  for (int mb = 0; mb < MT; ++mb)
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+      for (int x = 0; x < 4; ++x) acc[mb][q][x] = 0.0f;
+  const LaneOffsets o = lane_offsets<MT, GROUP, STAGES>(warp, lane);
+  bool ok = true;  // false once a wait gave up: no more MMAs, C or partials
+  int i = 0;
+  int split0 = -1, split1 = -1;  // tiles this run shares with other CTAs
+  int nsplit = 0;
+  for (long u = u0; u < u1;) {
+    const int nt = static_cast<int>(u / kblocks);
+    const int kb_begin = static_cast<int>(u - static_cast<long>(nt) * kblocks);
+    const int kb_end = static_cast<int>(min(u1 - static_cast<long>(nt) * kblocks,
+                                            static_cast<long>(kblocks)));
+    for (int kb = kb_begin; kb < kb_end; kb += KPS, ++i) {
+      const int s = i % STAGES;
+      const uint32_t ph = (i / STAGES) & 1u;
+      if (ok) ok = mbar_wait(bars + 8 * s, ph, abort_flag, status, wait_limit_ns);
+      if (ok)
+        compute_stage<MT, GROUP, STAGES>(ring + s * L::SLOT, o, lane, kb, min(KPS, kb_end - kb),
+                                         acc);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bars + 8 * (STAGES + s));
+    }
+    u = static_cast<long>(nt) * kblocks + kb_end;
+
+    float4 v[MT];
+#pragma unroll
+    for (int mb = 0; mb < MT; ++mb) {
+      v[mb].x = (acc[mb][0][0] + acc[mb][1][0]) + (acc[mb][2][0] + acc[mb][3][0]);
+      v[mb].y = (acc[mb][0][1] + acc[mb][1][1]) + (acc[mb][2][1] + acc[mb][3][1]);
+      v[mb].z = (acc[mb][0][2] + acc[mb][1][2]) + (acc[mb][2][2] + acc[mb][3][2]);
+      v[mb].w = (acc[mb][0][3] + acc[mb][1][3]) + (acc[mb][2][3] + acc[mb][3][3]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int x = 0; x < 4; ++x) acc[mb][q][x] = 0.0f;
+    }
+    if (kb_begin == 0 && kb_end == kblocks) {  // whole tile: this CTA writes C
+      if (ok)
+#pragma unroll
+        for (int mb = 0; mb < MT; ++mb) store_fragment(out, M, nt, warp, lane, mb, v[mb]);
+      continue;
+    }
+    // split tile: publish the partial now (no wait); tickets are taken once
+    // the whole run is done. Only a run's first and last segments can cut a
+    // tile, so there are at most two.
+    float4* mine = partials + static_cast<size_t>(c + nt) * SLOT4 + threadIdx.x * MT;
+#pragma unroll
+    for (int mb = 0; mb < MT; ++mb) __stcg(mine + mb, v[mb]);
+    if (nsplit++ == 0)
+      split0 = nt;
+    else
+      split1 = nt;
+  }
+  if (nsplit == 0) {  // CTA-uniform
+    if (out.count > 1) __threadfence_system();
+    return;
+  }
+  __threadfence();
+  if (!epi_bar_and(CTHREADS, ok)) return;  // also orders every partial before the tickets
+  if (threadIdx.x == 0) {
+    int last = 0;
+    for (int j = 0; j < nsplit; ++j) {
+      const long first_unit = static_cast<long>(j == 0 ? split0 : split1) * kblocks;
+      const int c_first = sk_owner(first_unit, grid, units);
+      const int c_last = sk_owner(first_unit + kblocks - 1, grid, units);
+      if (atomicAdd(&tickets[c_first], 1u) == static_cast<uint32_t>(c_last - c_first))
+        last |= 1 << j;
+    }
+    *last_flag = last;
+  }
+  epi_bar_sync(CTHREADS);
+  const int last = *last_flag;
+  if (last) __threadfence();
+  for (int j = 0; j < nsplit; ++j) {
+    if (!((last >> j) & 1)) continue;
+    const int nt = j == 0 ? split0 : split1;
+    const long first_unit = static_cast<long>(nt) * kblocks;
+    const int c_first = sk_owner(first_unit, grid, units);
+    const int nparts = sk_owner(first_unit + kblocks - 1, grid, units) - c_first + 1;
+    const float4* part = partials + static_cast<size_t>(c_first + nt) * SLOT4 + threadIdx.x * MT;
+    // sum the parts in run order; each batch of loads is issued before any
+    // of its adds
+    float4 sum[MT];
+    constexpr int BATCH = 8 / MT;
+#pragma unroll 1
+    for (int p0 = 0; p0 < nparts; p0 += BATCH) {
+      float4 q[BATCH][MT];
+#pragma unroll
+      for (int b = 0; b < BATCH; ++b)
+        if (p0 + b < nparts)
+#pragma unroll
+          for (int mb = 0; mb < MT; ++mb)
+            q[b][mb] = __ldcg(part + static_cast<size_t>(p0 + b) * SLOT4 + mb);
+#pragma unroll
+      for (int b = 0; b < BATCH; ++b) {
+        if (p0 + b >= nparts) break;
+#pragma unroll
+        for (int mb = 0; mb < MT; ++mb) {
+          if (p0 + b == 0) {
+            sum[mb] = q[b][mb];
+          } else {
+            sum[mb].x += q[b][mb].x;
+            sum[mb].y += q[b][mb].y;
+            sum[mb].z += q[b][mb].z;
+            sum[mb].w += q[b][mb].w;
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int mb = 0; mb < MT; ++mb) store_fragment(out, M, nt, warp, lane, mb, sum[mb]);
+    if (threadIdx.x == 0) tickets[c_first] = 0u;  // ready for the next launch
+  }
+  if (out.count > 1) __threadfence_system();  // peer copies are read by other GPUs
 }
 
 template <int MT, int GROUP>
@@ -454,6 +711,29 @@ cudaError_t launch_typed(const CUtensorMap& act_map, const uint8_t* tiles, const
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, act_map, tiles, scales, out, M, N, K, status,
                             wait_limit_ns);
+}
+
+template <int MT, int GROUP>
+cudaError_t launch_sk_typed(const CUtensorMap& act_map, const uint8_t* tiles,
+                            const __half* scales, const Outputs& out, int M, int N, int K,
+                            int grid, void* workspace, int* status,
+                            unsigned long long wait_limit_ns, cudaStream_t stream) {
+  constexpr int S = stages_for<MT, GROUP>();
+  using L = Layout<MT, GROUP, S>;
+  auto kernel = decode_sk_kernel<MT, GROUP, S>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         L::DYN);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  uint32_t* tickets = static_cast<uint32_t*>(workspace);
+  float4* partials =
+      reinterpret_cast<float4*>(static_cast<char*>(workspace) + tc::kTicketBytes);
+  kernel<<<grid, THREADS, L::DYN, stream>>>(act_map, tiles, scales, out, M, N, K, tickets,
+                                            partials, status, wait_limit_ns);
+  return cudaGetLastError();
 }
 
 // Tuning override for the cluster size (1-8), read once from
@@ -491,21 +771,77 @@ int choose_cluster(int N, int K, int sm_count) {
   return best;
 }
 
+// Schedule choice: kScheduleAuto lets the model in sk_plan decide;
+// kScheduleCluster / kScheduleStreamK force one (stream-K only with a large
+// enough workspace). Set by set_schedule; until then, I4G_DECODE_SCHEDULE
+// ("cluster" or "streamk") gives the initial value.
+std::atomic<int> g_schedule{-1};
+
+int schedule_mode() {
+  int v = g_schedule.load(std::memory_order_relaxed);
+  if (v >= 0) return v;
+  const char* e = std::getenv("I4G_DECODE_SCHEDULE");
+  int init = kScheduleAuto;
+  if (e && std::strcmp(e, "cluster") == 0) init = kScheduleCluster;
+  if (e && std::strcmp(e, "streamk") == 0) init = kScheduleStreamK;
+  int expected = -1;
+  g_schedule.compare_exchange_strong(expected, init, std::memory_order_relaxed);
+  return g_schedule.load(std::memory_order_relaxed);
+}
+
+void set_schedule(int mode) { g_schedule.store(mode, std::memory_order_relaxed); }
+
+SkPlan sk_plan(int M, int N, int K, int sm_count) {
+  SkPlan p{};
+  const long tiles = N / NCOL;
+  const long kblocks = K / BK;
+  const long units = tiles * kblocks;
+  const int grid = static_cast<int>(std::min<long>(units, static_cast<long>(CTAS_PER_SM) *
+                                                              sm_count));
+  if (grid < 1 || grid * 4 > static_cast<int>(tc::kTicketBytes)) return p;
+  const size_t slots = static_cast<size_t>(grid) + tiles - 1;
+  const size_t bytes = tc::kTicketBytes + slots * 16 *
+                                              (M <= 8 ? sk_slot_float4s<1>() : sk_slot_float4s<2>());
+  // Work of the busiest SM, in 64-k blocks of one column tile: the cluster
+  // schedule puts up to CTAS_PER_SM CTAs of ceil(kblocks / cluster) blocks on
+  // an SM, stream-K CTAS_PER_SM runs of ceil(units / grid) blocks. Measured
+  // on B200 (M = 1, g128, back-to-back calls): a block costs ~0.13 us on the
+  // busiest SM under either schedule, and stream-K's reduction through the
+  // workspace (partial stores, fence, ticket, last-arriver sum) costs ~3.5 us
+  // more than the cluster's reduction through distributed shared memory. So
+  // stream-K pays only when it takes more than ~27 blocks off the busiest SM
+  // (e.g. N = 28672, K = 8192: 256 -> 194 blocks, 36.3 -> 33.2 us; at N =
+  // 14336, K = 4096 the 14 blocks it saves do not: 12.6 vs 14.8 us).
+  const int cl = choose_cluster(N, K, sm_count);
+  const long ctas = tiles * cl;
+  const long most = (ctas + sm_count - 1) / sm_count;
+  const long cluster_work = most * ((kblocks + cl - 1) / cl);
+  const long per_sm = (static_cast<long>(grid) + sm_count - 1) / sm_count;
+  const long sk_work = per_sm * ((units + grid - 1) / grid);
+  p.grid = grid;
+  p.workspace_bytes = bytes;
+  const int mode = schedule_mode();
+  p.preferred = mode == kScheduleStreamK ||
+                (mode == kScheduleAuto && (cluster_work - sk_work) * 13 > 350);
+  return p;
+}
+
 template <int MT>
 cudaError_t launch_mt(const CUtensorMap& act_map, const uint8_t* tiles, const __half* scales,
-                      const Outputs& out, int M, int N, int K, int group, int cluster, int* status,
+                      const Outputs& out, int M, int N, int K, int group, int cluster,
+                      const SkPlan* sk, void* workspace, int* status,
                       unsigned long long wait_limit_ns, cudaStream_t stream) {
-  switch (group) {
-    case 32:
-      return launch_typed<MT, 32>(act_map, tiles, scales, out, M, N, K, cluster, status,
-                                  wait_limit_ns, stream);
-    case 64:
-      return launch_typed<MT, 64>(act_map, tiles, scales, out, M, N, K, cluster, status,
-                                  wait_limit_ns, stream);
-    default:
-      return launch_typed<MT, 128>(act_map, tiles, scales, out, M, N, K, cluster, status,
-                                   wait_limit_ns, stream);
-  }
+#define I4G_DEC_CASE(G)                                                                     \
+  if (group == G)                                                                           \
+    return sk ? launch_sk_typed<MT, G>(act_map, tiles, scales, out, M, N, K, sk->grid,     \
+                                       workspace, status, wait_limit_ns, stream)           \
+              : launch_typed<MT, G>(act_map, tiles, scales, out, M, N, K, cluster, status, \
+                                    wait_limit_ns, stream);
+  I4G_DEC_CASE(32)
+  I4G_DEC_CASE(64)
+  I4G_DEC_CASE(128)
+#undef I4G_DEC_CASE
+  return cudaErrorInvalidValue;
 }
 
 int rows_for(int M) { return M <= 8 ? 8 : 16; }
@@ -517,14 +853,17 @@ bool supported(int M, int K, int group) {
 }
 
 cudaError_t launch(const CUtensorMap& act_map, const uint8_t* tiles, const __half* scales,
-                   const Outputs& out, int M, int N, int K, int group, int sm_count, int* status,
+                   const Outputs& out, int M, int N, int K, int group, int sm_count,
+                   void* workspace, size_t workspace_bytes, int* status,
                    unsigned long long wait_limit_ns, cudaStream_t stream) {
-  const int cluster = choose_cluster(N, K, sm_count);
+  const SkPlan sk = sk_plan(M, N, K, sm_count);
+  const bool use_sk = workspace && sk.preferred && workspace_bytes >= sk.workspace_bytes;
+  const int cluster = use_sk ? 1 : choose_cluster(N, K, sm_count);
   if (M <= 8)
-    return launch_mt<1>(act_map, tiles, scales, out, M, N, K, group, cluster, status,
-                        wait_limit_ns, stream);
-  return launch_mt<2>(act_map, tiles, scales, out, M, N, K, group, cluster, status, wait_limit_ns,
-                      stream);
+    return launch_mt<1>(act_map, tiles, scales, out, M, N, K, group, cluster,
+                        use_sk ? &sk : nullptr, workspace, status, wait_limit_ns, stream);
+  return launch_mt<2>(act_map, tiles, scales, out, M, N, K, group, cluster,
+                      use_sk ? &sk : nullptr, workspace, status, wait_limit_ns, stream);
 }
 
 }  // namespace dec

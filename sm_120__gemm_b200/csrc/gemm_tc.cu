@@ -218,25 +218,6 @@ __device__ __forceinline__ void reduce_partials(const float4* base, const Output
   if constexpr (MULTI) __threadfence_system();  // peer copies are read by other GPUs
 }
 
-// Named barrier among the epilogue warps (barrier 1); `bar_and` also ANDs a
-// per-thread predicate across them.
-__device__ __forceinline__ void epi_bar_sync(int nthreads) {
-  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
-}
-
-__device__ __forceinline__ bool epi_bar_and(int nthreads, bool v) {
-  uint32_t out;
-  asm volatile(
-      "{\n\t.reg .pred pin, pout;\n\t"
-      "setp.ne.u32 pin, %1, 0;\n\t"
-      "bar.red.and.pred pout, 1, %2, pin;\n\t"
-      "selp.u32 %0, 1, 0, pout;\n\t}"
-      : "=r"(out)
-      : "r"(static_cast<uint32_t>(v)), "r"(nthreads)
-      : "memory");
-  return out != 0;
-}
-
 // Convert 32 fp32 accumulator columns of one lane into 16 packed halves.
 __device__ __forceinline__ void pack_half2(const uint32_t* v, uint32_t* out, int n) {
 #pragma unroll

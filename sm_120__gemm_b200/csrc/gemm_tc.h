@@ -21,8 +21,9 @@ struct Outputs {
 };
 
 namespace tc {
-// Ticket counters at the start of a split-K workspace, then the FP32 partials.
-constexpr size_t kTicketBytes = 1024;
+// Arrival counters (tickets) at the start of a split-K workspace, then the
+// FP32 partials; the decode kernel's stream-K schedule uses the same layout.
+constexpr size_t kTicketBytes = 4096;
 
 // Work schedule of one launch (device-visible): `full_tiles` whole tiles,
 // then the tail. chunks == 0: each of the following tiles split `split` ways
@@ -56,8 +57,22 @@ constexpr int MAX_M = 16;
 bool supported(int M, int K, int group);
 // Rows of the activation box the decode kernel's tensor map must use.
 int rows_for(int M);
+// Stream-K schedule of the decode kernel for a workspace (grid 0: not
+// possible); `preferred` when its busiest SM does less work than under the
+// cluster schedule.
+struct SkPlan {
+  int grid;
+  size_t workspace_bytes;
+  bool preferred;
+};
+SkPlan sk_plan(int M, int N, int K, int sm_count);
+constexpr int kScheduleAuto = 0, kScheduleCluster = 1, kScheduleStreamK = 2;
+void set_schedule(int mode);
+// Launches the stream-K schedule when `workspace` holds sk_plan's bytes and
+// it is preferred, else the cluster schedule (no workspace).
 cudaError_t launch(const CUtensorMap& act_map, const uint8_t* tiles, const __half* scales,
-                   const Outputs& out, int M, int N, int K, int group, int sm_count, int* status,
+                   const Outputs& out, int M, int N, int K, int group, int sm_count,
+                   void* workspace, size_t workspace_bytes, int* status,
                    unsigned long long wait_limit_ns, cudaStream_t stream);
 }  // namespace dec
 

@@ -128,6 +128,26 @@ __device__ __forceinline__ bool mbar_wait_lean(uint32_t bar, uint32_t parity,
   return mbar_wait_slow(bar, parity, abort, status, limit_ns);
 }
 
+// Named barrier 1 among `nthreads` threads (a subset of warps, e.g. those
+// that do not stream copies); `bar_and` also ANDs a per-thread predicate
+// across them.
+__device__ __forceinline__ void epi_bar_sync(int nthreads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
+
+__device__ __forceinline__ bool epi_bar_and(int nthreads, bool v) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred pin, pout;\n\t"
+      "setp.ne.u32 pin, %1, 0;\n\t"
+      "bar.red.and.pred pout, 1, %2, pin;\n\t"
+      "selp.u32 %0, 1, 0, pout;\n\t}"
+      : "=r"(out)
+      : "r"(static_cast<uint32_t>(v)), "r"(nthreads)
+      : "memory");
+  return out != 0;
+}
+
 // ------------------------------------------------------------ TMA / bulk
 
 __device__ __forceinline__ void prefetch_tensormap(const void* map) {

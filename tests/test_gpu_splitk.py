@@ -13,11 +13,9 @@ import torch
 
 import oracle
 from parity import fp32_report, gemm_report, make_inputs, u16
+from plans import TICKET_BYTES, expected_plan, expected_workspace
 
 pytestmark = pytest.mark.gpu
-
-TICKET_BYTES = 1024
-TILE_N = 128
 
 
 @pytest.fixture(scope="module")
@@ -29,36 +27,6 @@ def i4g():
     return m
 
 
-def expected_plan(M, N, K, budget=1 << 62):
-    """The schedule the host plans for this shape on cuda:0 (mirrors
-    make_plan and its cost model): (kind, workspace bytes, tile_m) with kind
-    "stream-k", "split<F>" or "whole"."""
-    sms = torch.cuda.get_device_properties(0).multi_processor_count
-    tile_m = 128 if M <= 128 else 256
-    tiles = -(-M // tile_m) * (N // TILE_N)
-    kb = K // 64
-    waves, rem = divmod(tiles, sms)
-    tile_bytes = tile_m * TILE_N * 4
-    if rem == 0 or rem * 4 > TICKET_BYTES:
-        return "whole", 0, tile_m
-    t_tile = kb * (0.45 if tile_m > 128 else 0.5)
-    best, plan = (waves + 1) * t_tile, ("whole", 0, tile_m)
-    f = min(4, sms // rem, kb // 8)
-    need = TICKET_BYTES + rem * f * tile_bytes
-    if f >= 2 and need <= budget and (waves + 1.0 / f) * t_tile + 12.0 < best:
-        best, plan = (waves + 1.0 / f) * t_tile + 12.0, (f"split{f}", need, tile_m)
-    run = rem * kb
-    chunks = min(sms, 3 * rem, run // 8)
-    if chunks > rem:
-        most = max((((t + 1) * kb) * chunks - 1) // run - ((t * kb + 1) * chunks - 1) // run + 1
-                   for t in range(rem))
-        need = TICKET_BYTES + (rem + chunks - 1) * tile_bytes
-        t_sk = (waves + rem / chunks) * t_tile + 20.0
-        if most <= 4 and run * chunks < 2**31 and need <= budget and t_sk < best:
-            plan = ("stream-k", need, tile_m)
-    return plan
-
-
 def fresh_workspace(i4g, M, N, K):
     n = i4g.gemm_workspace_size(M, N, K)
     return torch.zeros(max(n, 256), dtype=torch.uint8, device="cuda"), n
@@ -68,8 +36,8 @@ def fresh_workspace(i4g, M, N, K):
                                    (16, 4096, 4096), (4096, 4096, 448), (2048, 9472, 1024),
                                    (1024, 7168, 8192), (2048, 640, 8192)])
 def test_workspace_size(i4g, M, N, K):
-    kind, need, _ = expected_plan(M, N, K)
-    assert i4g.gemm_workspace_size(M, N, K) == (0 if M <= 16 else need), kind
+    kind, _, _ = expected_plan(M, N, K)
+    assert i4g.gemm_workspace_size(M, N, K) == expected_workspace(M, N, K), kind
 
 
 def split_case(i4g, M, N, K, grp, rows=None, fp32_out=False, seed=0):

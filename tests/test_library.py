@@ -63,6 +63,11 @@ def test_argument_checks_need_no_gpu(lib):
     assert lib.i4g_quantize(fake, fake, fake, 128, 127, 32, None) == -2
     assert lib.i4g_repack_umma(fake, fake, 96, 128, None) == -2
     assert lib.i4g_repack_128x32(fake, fake, fake, fake, 128, 100, 32, None) == -2
+    # decode schedule selector: unknown values are refused, known ones taken
+    assert lib.i4g_set_decode_schedule(3) == -9
+    assert lib.i4g_set_decode_schedule(-1) == -9
+    for mode in (2, 1, 0):
+        assert lib.i4g_set_decode_schedule(mode) == 0
 
 
 def test_shard_range_arithmetic():
