@@ -245,6 +245,25 @@ enum {
 };
 int i4g_set_decode_schedule(int schedule);
 
+/* ---- cross-GPU barrier (no counterpart in the reference) ------------------- */
+
+/* Stream-ordered barrier among `world` (<= 8) ranks, one per GPU, after
+ * i4g_gemm_to_peers: rank r owns an array of `world` 64-bit flags in device
+ * memory (zeroed once, before any rank's first barrier), mapped into every
+ * rank (CUDA IPC, i4g_ipc_*). peer_flags[q] is rank q's array as mapped here
+ * (peer_flags[rank] is not read). The call stores `epoch` into every peer's
+ * flag for this rank (release, system scope) and then waits until every
+ * peer has stored at least `epoch` into this rank's array (acquire), so the
+ * peer stores of the launches before it on every rank are visible to the
+ * launches after it. `epoch` must grow by one per barrier on every rank.
+ * The wait gives up after limit_ns (0: the GEMM kernels' 2 s limit) and then
+ * records I4G_ERR_TIMEOUT in the device status word (i4g_device_status),
+ * e.g. when a peer never arrives; it never faults or hangs the GPU. */
+int i4g_peer_barrier(unsigned long long* local_flags,
+                     unsigned long long* const* peer_flags, int world, int rank,
+                     unsigned long long epoch, unsigned long long limit_ns,
+                     void* stream);
+
 /* ---- device status --------------------------------------------------------- */
 
 /* Reads and clears this device's kernel status word (set when a device-side

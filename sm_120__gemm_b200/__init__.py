@@ -76,6 +76,8 @@ _SIGNATURES = {
     "i4g_device_status": [ctypes.POINTER(_i), _vp],
     "i4g_selftest_wait_timeout": [ctypes.c_ulonglong, _vp],
     "i4g_set_decode_schedule": [_i],
+    "i4g_peer_barrier": [_vp, ctypes.POINTER(_vp), _i, _i, ctypes.c_ulonglong, ctypes.c_ulonglong,
+                         _vp],
     "i4g_layout_version": [],
 }
 
@@ -307,6 +309,14 @@ def device_status(stream=None) -> int:
 
 def selftest_wait_timeout(limit_ns: int, stream=None) -> None:
     _call("i4g_selftest_wait_timeout", limit_ns, _stream(stream))
+
+
+def peer_barrier(local_flags: int, peer_flags, world: int, rank: int, epoch: int,
+                 limit_ns: int = 0, stream=None) -> None:
+    """C ABI i4g_peer_barrier: device pointers of this rank's flag array and
+    of every rank's array as mapped here (list indexed by rank)."""
+    arr = (_vp * world)(*[p or 0 for p in peer_flags])
+    _call("i4g_peer_barrier", local_flags, arr, world, rank, epoch, limit_ns, _stream(stream))
 
 
 DECODE_SCHEDULES = {"auto": 0, "cluster": 1, "streamk": 2}

@@ -410,7 +410,7 @@ def gather_sweep(iters):
         del w
         if rank == 0:
             print("M,world,kernel,gemm_us,gemm_plus_nccl_gather_us,fused_peer_store_us,"
-                  "nccl_gather_share")
+                  "nccl_gather_share,fused_equals_nccl")
         for M in (1, 16, 128, 1024, 4096, 16384):
             a = (torch.rand(M, K, generator=gen, device=dev) * 2 - 1).half()
             c_local = torch.empty(M, n_local, dtype=torch.float16, device=dev)
@@ -448,12 +448,20 @@ def gather_sweep(iters):
                 t = torch.tensor([b.elapsed_time(e) * 1e3 / iters], device=dev)
                 dist.all_reduce(t, op=dist.ReduceOp.MAX)
                 res.append(float(t.item()))
+            # the fused path's C must be the NCCL-gathered C bit for bit, on
+            # every rank
+            same = torch.ones(1, device=dev)
             if outs is not None:
+                e2e()
+                fused()
+                torch.cuda.synchronize()
+                same[0] = float(torch.equal(outs.view(M).view(torch.int16), out.view(torch.int16)))
+                dist.all_reduce(same, op=dist.ReduceOp.MIN)
                 outs.close()
             if rank == 0:
                 kern = "decode" if M <= 16 else "tcgen05"
                 print(f"{M},{world},{kern},{res[0]:.2f},{res[1]:.2f},{res[2]:.2f},"
-                      f"{(res[1] - res[0]) / res[1]:.3f}", flush=True)
+                      f"{(res[1] - res[0]) / res[1]:.3f},{int(same.item())}", flush=True)
             del a, c_local, gathered, out, outs
             torch.cuda.empty_cache()
         dist.barrier()

@@ -306,6 +306,38 @@ __global__ void wait_timeout_selftest_kernel(int* status, unsigned long long lim
   __syncthreads();
 }
 
+// Cross-GPU barrier over peer-mapped flag arrays (one 64-bit flag per rank in
+// every rank's array). Thread t < world (t != rank) stores `epoch` into rank
+// t's flag for this rank with release semantics at system scope, then waits
+// (acquire, system scope) until this rank's flag for rank t reaches `epoch`.
+// The stores a previous kernel on this stream made to peers (fenced at
+// system scope by that kernel) are therefore visible to a peer that has
+// seen the flag. Every wait is bounded by `limit_ns`; on timeout the status
+// word records it and the kernel returns.
+struct PeerFlagPtrs {
+  unsigned long long* p[i4g::kMaxOutputs];
+};
+
+__global__ void peer_barrier_kernel(unsigned long long* local, const __grid_constant__ PeerFlagPtrs peers, int world,
+                                    int rank, unsigned long long epoch, int* status,
+                                    unsigned long long limit_ns) {
+  const int t = static_cast<int>(threadIdx.x);
+  if (t >= world || t == rank) return;
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(peers.p[t] + rank), "l"(epoch)
+               : "memory");
+  const uint64_t t0 = i4g::global_timer_ns();
+  for (;;) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(local + t) : "memory");
+    if (v >= epoch) return;
+    if (i4g::global_timer_ns() - t0 > limit_ns) {
+      atomicExch(status, i4g::kStatusTimeout);
+      return;
+    }
+    __nanosleep(64);
+  }
+}
+
 }  // namespace
 
 extern "C" {
@@ -666,6 +698,31 @@ int i4g_set_decode_schedule(int schedule) {
                 "decode schedule codes");
   i4g::dec::set_schedule(schedule);
   return I4G_OK;
+}
+
+int i4g_peer_barrier(unsigned long long* local_flags, unsigned long long* const* peer_flags,
+                     int world, int rank, unsigned long long epoch,
+                     unsigned long long limit_ns, void* stream) {
+  if (!local_flags || !peer_flags) return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
+  if (world < 1 || world > i4g::kMaxOutputs || rank < 0 || rank >= world)
+    return fail(I4G_ERR_SHAPE, "rank %d of world %d (at most %d ranks)", rank, world,
+                i4g::kMaxOutputs);
+  if (epoch == 0) return fail(I4G_ERR_SHAPE, "epoch must be positive");
+  if (!aligned(local_flags, 8)) return fail(I4G_ERR_ALIGNMENT, "flags must be 8-byte aligned");
+  PeerFlagPtrs peers{};
+  for (int r = 0; r < world; ++r) {
+    if (r == rank) continue;
+    if (!peer_flags[r]) return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
+    if (!aligned(peer_flags[r], 8)) return fail(I4G_ERR_ALIGNMENT, "flags must be 8-byte aligned");
+    peers.p[r] = peer_flags[r];
+  }
+  DeviceInfo* dev = nullptr;
+  int st = current_device(&dev);
+  if (st != I4G_OK) return st;
+  const unsigned long long limit = limit_ns ? limit_ns : g_wait_limit_ns;
+  peer_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      local_flags, peers, world, rank, epoch, dev->status_word, limit);
+  return finish(cudaGetLastError(), "peer barrier launch");
 }
 
 int i4g_selftest_wait_timeout(unsigned long long limit_ns, void* stream) {

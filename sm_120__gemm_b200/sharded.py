@@ -16,7 +16,8 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
-from . import ipc_close, ipc_handle, ipc_open, launch_final_to_peers, workspace_for
+from . import (ipc_close, ipc_handle, ipc_open, launch_final_to_peers, peer_barrier,
+               workspace_for)
 from .linear import QuantizedLinear
 
 
@@ -45,36 +46,56 @@ class PeerOutputs:
     """Every rank's full C buffer ([max_m, N] FP16), mapped into every rank
     (CUDA IPC, plain peer-to-peer mappings), so that one GEMM launch per rank
     can write its column block into all of them: the all-gather fused into
-    the GEMM epilogue. Collective: every rank of `group` constructs it."""
+    the GEMM epilogue. The same allocation holds this rank's barrier flags
+    (one 64-bit flag per rank, after C), which the peers set through their
+    mappings (``i4g_peer_barrier``). Collective: every rank of `group`
+    constructs it."""
+
+    FLAG_BYTES = 256  # room for 32 ranks; the barrier kernel takes up to 8
 
     def __init__(self, max_m: int, N: int, device, group=None):
         self.max_m, self.N, self.group = max_m, N, group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
-        self.buf = torch.empty(max_m * N, dtype=torch.float16, device=device)
-        mine = ipc_handle(self.buf)
+        c_bytes = max_m * N * 2
+        self._flag_off = (c_bytes + 255) // 256 * 256
+        self._raw = torch.empty(self._flag_off + self.FLAG_BYTES, dtype=torch.uint8,
+                                device=device)
+        self._raw[self._flag_off:].zero_()
+        # the flags are zero before any peer can reach them (the handle
+        # exchange below is the first point at which a peer could)
+        torch.cuda.synchronize(device)
+        self.buf = self._raw[:c_bytes].view(torch.float16)
+        mine = ipc_handle(self._raw)
         handles = [None] * self.world
         dist.all_gather_object(handles, mine, group=group)
         self._opened = []
         peers = []
+        self._flag_ptrs = [0] * self.world
         for r in range(self.world):
             if r == self.rank:
+                self._flag_ptrs[r] = self._raw.data_ptr() + self._flag_off
                 continue
             h, off = handles[r]
             base = ipc_open(h)
             self._opened.append(base)
             peers.append(base + off)
+            self._flag_ptrs[r] = base + off + self._flag_off
         # this GPU's copy first, then the peers' (the kernel writes them in order)
         self.dsts = [self.buf.data_ptr()] + peers
-        self._flag = torch.zeros(1, dtype=torch.float32, device=device)
+        self._epoch = 0
 
     def view(self, M: int) -> torch.Tensor:
         return self.buf[: M * self.N].view(M, self.N)
 
-    def barrier(self) -> None:
-        """Stream-ordered cross-rank barrier: after it, every rank's launch
-        (and its peer stores) has completed."""
-        dist.all_reduce(self._flag, group=self.group)
+    def barrier(self, stream=None) -> None:
+        """Stream-ordered cross-rank barrier (a flag per rank pair over the
+        peer mappings): after it, every rank's launches before it (and their
+        peer stores) have completed. Every rank calls it the same number of
+        times."""
+        self._epoch += 1
+        peer_barrier(self._flag_ptrs[self.rank], self._flag_ptrs, self.world, self.rank,
+                     self._epoch, stream=stream)
 
     def close(self) -> None:
         torch.cuda.synchronize()
@@ -119,5 +140,5 @@ class ColumnParallelLinear:
         ws = workspace_for(M, loc.N, loc.K, a.device, stream)
         launch_final_to_peers(a, loc.tiles, loc.scales, outs.dsts, self.N, self.n0, M, loc.N,
                               loc.K, loc.group, ws, stream)
-        outs.barrier()
+        outs.barrier(stream)
         return outs.view(M)

@@ -51,6 +51,14 @@ def _worker(rank, world, port, q, M, N, K, group):
         torch.cuda.synchronize()
         ok = (bool(torch.equal(c.view(torch.int16), ref.view(torch.int16))) and
               bool(torch.equal(c2.view(torch.int16), ref.view(torch.int16))))
+        # more calls through the same buffers (barrier epochs 2, 3, ...), each
+        # with new activations, read right after the barrier
+        for it in range(3):
+            a_it = (torch.rand(M, K, generator=g) * 2 - 1).half().cuda()
+            got = cp.forward_to_peers(a_it, outs).clone()
+            ok = ok and bool(torch.equal(got.view(torch.int16), full(a_it).view(torch.int16)))
+        torch.cuda.synchronize()
+        ok = ok and i4g.device_status() == 0
         outs.close()
         flags = [None] * world
         dist.all_gather_object(flags, ok)

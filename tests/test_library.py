@@ -63,6 +63,12 @@ def test_argument_checks_need_no_gpu(lib):
     assert lib.i4g_quantize(fake, fake, fake, 128, 127, 32, None) == -2
     assert lib.i4g_repack_umma(fake, fake, 96, 128, None) == -2
     assert lib.i4g_repack_128x32(fake, fake, fake, fake, 128, 100, 32, None) == -2
+    # peer barrier argument checks come before any device access
+    flags = (ctypes.c_void_p * 2)(fake, fake)
+    assert lib.i4g_peer_barrier(None, flags, 2, 0, 1, 0, None) == -1
+    assert lib.i4g_peer_barrier(fake, flags, 9, 0, 1, 0, None) == -2
+    assert lib.i4g_peer_barrier(fake, flags, 2, 2, 1, 0, None) == -2
+    assert lib.i4g_peer_barrier(fake, flags, 2, 0, 0, 0, None) == -2
     # decode schedule selector: unknown values are refused, known ones taken
     assert lib.i4g_set_decode_schedule(3) == -9
     assert lib.i4g_set_decode_schedule(-1) == -9
