@@ -3,10 +3,12 @@
 Each rank owns an N/world slice of the packed weights and scales (a
 contiguous byte range of the tile and scale layouts, see ``shard_range``);
 the activations A are replicated. The GEMM itself needs no communication.
-Only when one rank needs the full C does a collective run: an all-gather of
-the FP16 C column blocks (NCCL over NVLink on GPUs, gloo on CPU in tests),
-which yields the rank-major ``[world][M][N/world]`` buffer that
-``assemble_columns`` turns into row-major ``[M][N]``.
+When a rank needs the full C, either an all-gather of the FP16 C column
+blocks runs (NCCL over NVLink on GPUs, gloo on CPU in tests), which yields
+the rank-major ``[world][M][N/world]`` buffer that ``assemble_columns`` turns
+into row-major ``[M][N]``, or (``forward_to_peers``) every rank's GEMM
+stores its columns straight into every rank's C over peer mappings and a
+flag barrier (``i4g_peer_barrier``) orders the readers.
 
 The reference has no multi-GPU path; this is the north star's harness for
 configs 3 and 4 (M=8192, K=8192, N=28672; K=8192, N=57344, g64, 8 GPUs).
