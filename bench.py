@@ -385,9 +385,17 @@ def cpu_sample(rows, threads, group=128, seed=0):
 
 
 def cpu_baseline(args, sample_rows):
+    """The reference's CPU path on a bounded row sample sized to about
+    args.cpu_seconds of CPU work: a first sample of `sample_rows` rows
+    calibrates the time per row, then the timed sample is taken."""
     threads = _cpu_threads()
     rows = max(sample_rows, threads)
     t_deq, t_rows, kind = cpu_sample(rows, threads)
+    per_row = t_rows / rows
+    want = max(rows, min(M_HEAD, int((args.cpu_seconds - t_deq) / max(per_row, 1e-9))))
+    if want > rows:
+        rows = want
+        t_deq, t_rows, kind = cpu_sample(rows, threads, seed=1)
     t_full = t_deq + t_rows * (M_HEAD / rows)
     value = flops(M_HEAD, N_HEAD, K_HEAD) / t_full / 1e12
     return {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
@@ -438,6 +446,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-rows", type=int, default=64)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="CPU work of the cpu_baseline sample (rows are chosen to fit it)")
     ap.add_argument("--schedule", choices=["split", "whole"], default="split",
                     help="split: split-K the last partial wave through a workspace; "
                          "whole: whole output tiles only (i4g_gemm)")

@@ -165,7 +165,9 @@ int i4g_gemm_variant(const void* A, const uint8_t* tiles, const void* scales,
  * best schedule that fits (equal splits, or whole tiles; NULL: whole tiles;
  * the decode kernel: its cluster schedule). Launches sharing one workspace
  * must be ordered (one stream); concurrent launches on the same workspace
- * race. */
+ * race. A launch that gave up on a device-side wait (i4g_device_status
+ * reports I4G_ERR_TIMEOUT) may leave counters non-zero: zero the workspace
+ * again before reusing it (i4g_gemm_static_scratch does this itself). */
 int i4g_gemm_workspace_size(int M, int N, int K, size_t* bytes);
 int i4g_gemm_ws(const void* A, const uint8_t* tiles, const void* scales, void* C,
                 int M, int N, int K, int group, void* workspace,
