@@ -690,13 +690,9 @@ cudaError_t launch_typed(const CUtensorMap& act_map, const uint8_t* tiles, const
   constexpr int S = stages_for<MT, GROUP>();
   using L = Layout<MT, GROUP, S>;
   auto kernel = decode_kernel<MT, GROUP, S>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         L::DYN);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static std::atomic<uint64_t> configured{0};  // devices set, per instantiation
+  cudaError_t e = ensure_dynamic_smem(kernel, L::DYN, configured);
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((N / NCOL) * cluster);
   cfg.blockDim = dim3(THREADS);
@@ -721,13 +717,9 @@ cudaError_t launch_sk_typed(const CUtensorMap& act_map, const uint8_t* tiles,
   constexpr int S = stages_for<MT, GROUP>();
   using L = Layout<MT, GROUP, S>;
   auto kernel = decode_sk_kernel<MT, GROUP, S>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         L::DYN);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static std::atomic<uint64_t> configured{0};  // devices set, per instantiation
+  cudaError_t e = ensure_dynamic_smem(kernel, L::DYN, configured);
+  if (e != cudaSuccess) return e;
   uint32_t* tickets = static_cast<uint32_t*>(workspace);
   float4* partials =
       reinterpret_cast<float4*>(static_cast<char*>(workspace) + tc::kTicketBytes);

@@ -740,13 +740,9 @@ cudaError_t launch_impl(const CUtensorMap& act_map, const uint8_t* tiles, const 
                         int* status, unsigned long long wait_limit_ns, cudaStream_t stream) {
   using L = Cfg<TILE_M>;
   auto kernel = gemm_tc_kernel<TILE_M, GROUP, OUT>;
-  static bool configured = false;  // per instantiation; idempotent attribute
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         L::DYN_BYTES);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static std::atomic<uint64_t> configured{0};  // devices set, per instantiation
+  cudaError_t e = ensure_dynamic_smem(kernel, L::DYN_BYTES, configured);
+  if (e != cudaSuccess) return e;
   const int grid = plan.grid;
   uint32_t* tickets = static_cast<uint32_t*>(workspace);
   float* partials = workspace ? reinterpret_cast<float*>(static_cast<char*>(workspace) +

@@ -4,9 +4,27 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <atomic>
 #include <cstdint>
 
 namespace i4g {
+
+// Raises `kernel`'s dynamic shared-memory limit to `bytes` on the current
+// device, once per device: the attribute belongs to the kernel's instance on
+// each device, so a process that drives several GPUs sets it on every one.
+// `done` is the kernel's bitmask of devices already set (thread-safe;
+// setting the attribute twice is harmless).
+template <typename Kernel>
+cudaError_t ensure_dynamic_smem(Kernel kernel, int bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = (dev >= 0 && dev < 64) ? (uint64_t{1} << dev) : 0;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_release);
+  return e;
+}
 
 // Where a launch writes C: `count` copies (this GPU's, then peers' through
 // peer-mapped pointers), each a row-major [M][ldc] matrix of which the launch
