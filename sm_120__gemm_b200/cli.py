@@ -372,7 +372,8 @@ def configs(iters, csv_path=""):
         tf = flops / (best * 1e-6) / 1e12
         gbs = nbytes / (best * 1e-6) / 1e9
         kernel = "decode (mma.sync)" if M <= 16 else "tcgen05"
-        sched = "-" if M <= 16 else ("split-K tail" if ws is not None else "whole tiles")
+        # decode: cluster or stream-K, as i4g_set_decode_schedule's automatic choice picks
+        sched = "auto" if M <= 16 else ("split-K tail" if ws is not None else "whole tiles")
         lines.append(f"{label},{M},{N},{K},{g},{kernel},{sched},{best:.2f},{tf:.1f},{gbs:.0f},"
                      f"{tf / pk_tf:.3f},{gbs / pk_bw:.3f}")
         print(lines[-1], flush=True)
