@@ -229,6 +229,35 @@ int i4g_shard_range(int K, int N, int group, int world, int rank,
                     size_t* tile_offset, size_t* scale_offset,
                     int* n0, int* n1);
 
+/* ---- launch plan query (no counterpart in the reference) ------------------ */
+
+/* The kernel and schedule a GEMM of this shape would run on a device with
+ * sm_count SMs when given workspace_bytes of workspace (0: none), computed on
+ * the host without touching a device, by the same planners the launches use
+ * (and under the current i4g_set_decode_schedule choice).
+ *   *kernel:   I4G_PLAN_KERNEL_TC256 / _TC128 (tcgen05, 256- or 128-row
+ *              activation tiles) or I4G_PLAN_KERNEL_DECODE
+ *   *schedule: tcgen05: WHOLE (*param = grid), SPLIT (*param = ways each
+ *              tail tile is split), STREAMK (*param = tail shares);
+ *              decode: CLUSTER (*param = cluster size), STREAMK (*param =
+ *              grid)
+ *   *bytes:    workspace bytes that schedule uses
+ * fp32_out: as i4g_gemm_fp32 (never the decode kernel). */
+enum {
+  I4G_PLAN_KERNEL_TC256 = 0,
+  I4G_PLAN_KERNEL_TC128 = 1,
+  I4G_PLAN_KERNEL_DECODE = 2
+};
+enum {
+  I4G_PLAN_WHOLE = 0,
+  I4G_PLAN_SPLIT = 1,
+  I4G_PLAN_STREAMK = 2,
+  I4G_PLAN_CLUSTER = 3
+};
+int i4g_plan(int M, int N, int K, int group, int fp32_out, int sm_count,
+             size_t workspace_bytes, int* kernel, int* schedule, int* param,
+             size_t* bytes);
+
 /* ---- decode schedule (no counterpart in the reference) --------------------- */
 
 /* The decode kernel (M <= 16, FP16 C) has two schedules: the cluster schedule

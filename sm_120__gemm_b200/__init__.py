@@ -76,6 +76,8 @@ _SIGNATURES = {
     "i4g_device_status": [ctypes.POINTER(_i), _vp],
     "i4g_selftest_wait_timeout": [ctypes.c_ulonglong, _vp],
     "i4g_set_decode_schedule": [_i],
+    "i4g_plan": [_i, _i, _i, _i, _i, _i, ctypes.c_size_t, ctypes.POINTER(_i), ctypes.POINTER(_i),
+                 ctypes.POINTER(_i), ctypes.POINTER(ctypes.c_size_t)],
     "i4g_peer_barrier": [_vp, ctypes.POINTER(_vp), _i, _i, ctypes.c_ulonglong, ctypes.c_ulonglong,
                          _vp],
     "i4g_layout_version": [],
@@ -317,6 +319,23 @@ def peer_barrier(local_flags: int, peer_flags, world: int, rank: int, epoch: int
     of every rank's array as mapped here (list indexed by rank)."""
     arr = (_vp * world)(*[p or 0 for p in peer_flags])
     _call("i4g_peer_barrier", local_flags, arr, world, rank, epoch, limit_ns, _stream(stream))
+
+
+PLAN_KERNELS = {0: "tcgen05/256", 1: "tcgen05/128", 2: "decode"}
+PLAN_SCHEDULES = {0: "whole", 1: "split", 2: "stream-k", 3: "cluster"}
+
+
+def plan(M: int, N: int, K: int, group: int, sm_count: int, workspace_bytes: int = 0,
+         fp32_out: bool = False) -> dict:
+    """C ABI i4g_plan: the kernel and schedule this shape would run with
+    `workspace_bytes` of workspace on a device with `sm_count` SMs (no
+    device needed)."""
+    k, s, p = _i(), _i(), _i()
+    b = ctypes.c_size_t()
+    _call("i4g_plan", M, N, K, group, int(fp32_out), sm_count, workspace_bytes, ctypes.byref(k),
+          ctypes.byref(s), ctypes.byref(p), ctypes.byref(b))
+    return {"kernel": PLAN_KERNELS[k.value], "schedule": PLAN_SCHEDULES[s.value],
+            "param": p.value, "workspace_bytes": b.value}
 
 
 DECODE_SCHEDULES = {"auto": 0, "cluster": 1, "streamk": 2}

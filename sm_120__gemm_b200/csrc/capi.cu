@@ -688,6 +688,48 @@ int i4g_device_status(int* out, void* stream) {
   return I4G_OK;
 }
 
+int i4g_plan(int M, int N, int K, int group, int fp32_out, int sm_count,
+             size_t workspace_bytes, int* kernel, int* schedule, int* param, size_t* bytes) {
+  if (!kernel || !schedule || !param || !bytes)
+    return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
+  int st = check_shape(M, N, K);
+  if (st != I4G_OK) return st;
+  st = check_group(K, group, true);
+  if (st != I4G_OK) return st;
+  if (sm_count < 1 || sm_count > 4096) return fail(I4G_ERR_SHAPE, "sm_count %d", sm_count);
+  // the same choices as gemm_common and the kernels' launchers
+  if (!fp32_out && i4g::dec::supported(M, K, group)) {
+    *kernel = I4G_PLAN_KERNEL_DECODE;
+    const i4g::dec::SkPlan sk = i4g::dec::sk_plan(M, N, K, sm_count);
+    if (workspace_bytes > 0 && sk.preferred && workspace_bytes >= sk.workspace_bytes) {
+      *schedule = I4G_PLAN_STREAMK;
+      *param = sk.grid;
+      *bytes = sk.workspace_bytes;
+    } else {
+      *schedule = I4G_PLAN_CLUSTER;
+      *param = i4g::dec::choose_cluster(N, K, sm_count);
+      *bytes = 0;
+    }
+    return I4G_OK;
+  }
+  const int tile_m =
+      tile_m_override() ? tile_m_override() : i4g::tc::choose_tile_m(M, N, sm_count);
+  const i4g::tc::Plan plan = i4g::tc::make_plan(tile_m, M, N, K, sm_count, workspace_bytes, true);
+  *kernel = tile_m == 128 ? I4G_PLAN_KERNEL_TC128 : I4G_PLAN_KERNEL_TC256;
+  *bytes = plan.workspace_bytes;
+  if (plan.sched.chunks > 0) {
+    *schedule = I4G_PLAN_STREAMK;
+    *param = plan.sched.chunks;
+  } else if (plan.sched.split > 1) {
+    *schedule = I4G_PLAN_SPLIT;
+    *param = plan.sched.split;
+  } else {
+    *schedule = I4G_PLAN_WHOLE;
+    *param = plan.grid;
+  }
+  return I4G_OK;
+}
+
 int i4g_set_decode_schedule(int schedule) {
   if (schedule != I4G_DECODE_AUTO && schedule != I4G_DECODE_CLUSTER &&
       schedule != I4G_DECODE_STREAMK)

@@ -84,6 +84,8 @@ struct SkPlan {
   bool preferred;
 };
 SkPlan sk_plan(int M, int N, int K, int sm_count);
+// Cluster size of the cluster schedule (K split of each column tile).
+int choose_cluster(int N, int K, int sm_count);
 constexpr int kScheduleAuto = 0, kScheduleCluster = 1, kScheduleStreamK = 2;
 void set_schedule(int mode);
 // Launches the stream-K schedule when `workspace` holds sk_plan's bytes and

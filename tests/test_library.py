@@ -69,6 +69,14 @@ def test_argument_checks_need_no_gpu(lib):
     assert lib.i4g_peer_barrier(fake, flags, 9, 0, 1, 0, None) == -2
     assert lib.i4g_peer_barrier(fake, flags, 2, 2, 1, 0, None) == -2
     assert lib.i4g_peer_barrier(fake, flags, 2, 0, 0, 0, None) == -2
+    # plan query: no device needed, arguments checked
+    k, sch, prm, b = ctypes.c_int(), ctypes.c_int(), ctypes.c_int(), ctypes.c_size_t()
+    ref = [ctypes.byref(x) for x in (k, sch, prm, b)]
+    assert lib.i4g_plan(64, 128, 128, 64, 0, 148, 0, None, *ref[1:]) == -1
+    assert lib.i4g_plan(64, 100, 128, 64, 0, 148, 0, *ref) == -2
+    assert lib.i4g_plan(64, 128, 128, 96, 0, 148, 0, *ref) == -3
+    assert lib.i4g_plan(64, 128, 128, 64, 0, 0, 0, *ref) == -2
+    assert lib.i4g_plan(64, 128, 128, 64, 0, 148, 0, *ref) == 0
     # decode schedule selector: unknown values are refused, known ones taken
     assert lib.i4g_set_decode_schedule(3) == -9
     assert lib.i4g_set_decode_schedule(-1) == -9

@@ -1,0 +1,72 @@
+"""The host planners, through i4g_plan (no device needed), against their
+Python mirrors in tests/plans.py: which kernel, which schedule, its
+parameter and its workspace, over a sweep of shapes, two SM counts and three
+workspace sizes. The GPU tests rely on the same mirrors to know which
+schedule a shape runs."""
+import pytest
+
+from plans import TICKET_BYTES, TILE_N, decode_cluster, expected_decode_plan, expected_plan
+
+MS = (1, 5, 8, 9, 16, 17, 100, 128, 129, 300, 512, 1000, 1024, 4096, 8192)
+NS = (128, 640, 1024, 4096, 7168, 14336, 28672)
+KS = (64, 448, 1024, 4096, 8192, 14336)
+BUDGETS = (0, 20 << 20, 1 << 40)
+
+
+@pytest.fixture(scope="module")
+def i4g():
+    import sm_120__gemm_b200 as m
+    m.load()
+    m.set_decode_schedule("auto")
+    return m
+
+
+@pytest.mark.parametrize("sms", [148, 132])
+def test_plan_query_matches_the_mirrors(i4g, sms):
+    checked = 0
+    for M in MS:
+        for N in NS:
+            for K in KS:
+                for budget in BUDGETS:
+                    got = i4g.plan(M, N, K, 64, sms, budget)
+                    if M <= 16:
+                        pref, grid, need = expected_decode_plan(M, N, K, sms=sms)
+                        if budget > 0 and pref and budget >= need:
+                            want = ("decode", "stream-k", grid, need)
+                        else:
+                            want = ("decode", "cluster", decode_cluster(N, K, sms), 0)
+                    else:
+                        kind, need, tile_m = expected_plan(M, N, K, budget=budget, sms=sms)
+                        kern = f"tcgen05/{tile_m}"
+                        if kind == "whole":
+                            tiles = -(-M // tile_m) * (N // TILE_N)
+                            want = (kern, "whole", min(tiles, sms), 0)
+                        elif kind.startswith("split"):
+                            want = (kern, "split", int(kind[5:]), need)
+                        else:
+                            tiles = -(-M // tile_m) * (N // TILE_N)
+                            rem = tiles % sms
+                            chunks = (need - TICKET_BYTES) // (tile_m * TILE_N * 4) - rem + 1
+                            want = (kern, "stream-k", chunks, need)
+                    have = (got["kernel"], got["schedule"], got["param"], got["workspace_bytes"])
+                    assert have == want, (M, N, K, budget, sms, have, want)
+                    checked += 1
+    assert checked == len(MS) * len(NS) * len(KS) * len(BUDGETS)
+
+
+def test_forced_decode_schedules(i4g):
+    try:
+        i4g.set_decode_schedule("streamk")
+        _, grid, need = expected_decode_plan(4, 14336, 4096, sms=148, schedule="streamk")
+        assert i4g.plan(4, 14336, 4096, 128, 148, need) == {
+            "kernel": "decode", "schedule": "stream-k", "param": grid, "workspace_bytes": need}
+        # too small a workspace: the cluster schedule
+        assert i4g.plan(4, 14336, 4096, 128, 148, need - 1)["schedule"] == "cluster"
+        i4g.set_decode_schedule("cluster")
+        assert i4g.plan(1, 28672, 8192, 128, 148, 1 << 40)["schedule"] == "cluster"
+    finally:
+        i4g.set_decode_schedule("auto")
+
+
+def test_fp32_output_never_uses_the_decode_kernel(i4g):
+    assert i4g.plan(1, 4096, 4096, 128, 148, 0, fp32_out=True)["kernel"] == "tcgen05/128"
