@@ -24,7 +24,7 @@ import sys
 
 import torch
 
-from . import (QuantizedLinear, launch_dequantize, launch_final, launch_final_fp32,
+from . import (QuantizedLinear, launch_dequantize, launch_final, launch_final_fp32, plan,
                launch_inverse_repack_128x32, launch_inverse_repack_umma, launch_quantize,
                launch_repack_128x32, launch_repack_mma_128x32, launch_repack_mma_pair_128x32,
                launch_repack_scales_128, launch_repack_umma, launch_quantize_repack,
@@ -371,9 +371,11 @@ def configs(iters, csv_path=""):
         nbytes = 2 * M * K + K * N // 2 + 2 * N * (K // g) + 2 * M * N
         tf = flops / (best * 1e-6) / 1e12
         gbs = nbytes / (best * 1e-6) / 1e9
-        kernel = "decode (mma.sync)" if M <= 16 else "tcgen05"
-        # decode: cluster or stream-K, as i4g_set_decode_schedule's automatic choice picks
-        sched = "auto" if M <= 16 else ("split-K tail" if ws is not None else "whole tiles")
+        # the kernel and schedule these calls ran (the planners, via i4g_plan)
+        info = plan(M, N, K, g, torch.cuda.get_device_properties(0).multi_processor_count,
+                    0 if ws is None else ws.numel())
+        kernel = info["kernel"]
+        sched = f'{info["schedule"]} ({info["param"]})'
         lines.append(f"{label},{M},{N},{K},{g},{kernel},{sched},{best:.2f},{tf:.1f},{gbs:.0f},"
                      f"{tf / pk_tf:.3f},{gbs / pk_bw:.3f}")
         print(lines[-1], flush=True)
