@@ -573,8 +573,11 @@ int i4g_gemm_static_scratch(const void* A, const uint8_t* tiles, const void* sca
     need = i4g::tc::make_plan(tc_tile_m(M, N, dev), M, N, K, dev->sm_count, SIZE_MAX, true)
                .workspace_bytes;
   } else {
+    // the decode kernel's stream-K schedule when its workspace fits the
+    // static scratch; otherwise its cluster schedule, which needs none
     const i4g::dec::SkPlan sk = i4g::dec::sk_plan(M, N, K, dev->sm_count);
-    if (sk.preferred) need = sk.workspace_bytes;
+    if (sk.preferred && sk.workspace_bytes <= i4g::static_scratch_bytes())
+      need = sk.workspace_bytes;
   }
   if (need > i4g::static_scratch_bytes()) {
     std::snprintf(t_last_error, sizeof(t_last_error),
