@@ -60,3 +60,21 @@ def fp32_report(got32: np.ndarray, ref32: np.ndarray, abs32: np.ndarray, K: int)
     bound = gamma * abs32.astype(np.float64) + 1e-30
     return {"ok": bool((diff <= bound).all()), "max_abs": float(diff.max()),
             "max_rel_to_bound": float((diff / bound).max())}
+
+
+def fp64_attribution(a16_rows: np.ndarray, deq16: np.ndarray, got16: np.ndarray,
+                     ref32: np.ndarray) -> dict:
+    """Attribute the residual against an FP64 oracle: the dequantized FP16
+    products (exact in FP64) summed in FP64 and rounded once to FP16 give the
+    best FP16 answer for each output; this output and the reference's FP32
+    path (rounded to FP16) are both measured from it in ulps. Where the two
+    differ by more than an ulp, this says which one the summation order put
+    further from the exact product."""
+    a = oracle.h2f(a16_rows).astype(np.float64)
+    w = oracle.h2f(deq16).astype(np.float64)
+    truth16 = (a @ w).astype(np.float16).view(np.uint16)
+    ours = oracle.ulp_distance(got16, truth16)
+    ref = oracle.ulp_distance(oracle.f2h(ref32), truth16)
+    return {"fp64_max_ulp_ours": int(ours.max()), "fp64_max_ulp_ref": int(ref.max()),
+            "fp64_outputs_closer_ours": int((ours < ref).sum()),
+            "fp64_outputs_closer_ref": int((ref < ours).sum())}

@@ -12,7 +12,7 @@ import torch
 
 import oracle
 from conftest import golden_names, load_golden
-from parity import fp32_report, gemm_report, make_inputs, u16
+from parity import fp32_report, fp64_attribution, gemm_report, make_inputs, u16
 
 pytestmark = pytest.mark.gpu
 
@@ -176,6 +176,7 @@ def run_case(i4g, M, N, K, grp, rows=None, a_dist="uniform", variant=0, seed=0):
     ref32 = oracle.gemm_rows(a16, deq, M, N, K, rows=rows, threads=8)
     abs32 = oracle.abs_gemm_rows(a16, deq, M, N, K, rows=rows)
     rep = gemm_report(got[rows], ref32, abs32, K)
+    rep.update(fp64_attribution(a16[rows], deq, got[rows], ref32))  # reported, not gated
     return rep, c
 
 

@@ -105,3 +105,18 @@ def test_compare_half_matches_reference_formula(oracle_mod):
     m = oracle_mod.compare_half(got, ref)
     assert m.max_abs > 0 and m.relative_l2 < 1e-2
     assert oracle_mod.compare_half(ref, ref).max_abs == 0
+
+
+@pytest.mark.parametrize("name", golden_names("gemm_"))
+def test_fp64_attribution_of_the_reference_path(oracle_mod, name):
+    """The FP64 attribution used by the GPU parity reports: the reference's
+    own FP32 path, judged against the FP64 oracle, is the same distance from
+    it as itself (sanity) and at most a few ulps from it on these cases."""
+    from parity import fp64_attribution
+    g = load_golden(name)
+    M, N, K, grp = g["M"], g["N"], g["K"], g["group"]
+    deq = oracle_mod.dequantize(g["packed"], g["scales"], K, N, grp)
+    rep = fp64_attribution(g["a"], deq, g["c16"], g["c32"])
+    assert rep["fp64_max_ulp_ours"] == rep["fp64_max_ulp_ref"]
+    assert rep["fp64_outputs_closer_ours"] == rep["fp64_outputs_closer_ref"] == 0
+    assert rep["fp64_max_ulp_ref"] <= 8, rep
