@@ -22,12 +22,15 @@ import os
 import threading
 
 __all__ = [
-    "I4GError", "load", "launch_quantize", "launch_dequantize", "launch_repack_128x32",
-    "launch_inverse_repack_128x32", "launch_repack_mma_128x32",
+    "I4GError", "load", "launch_quantize", "launch_quantize_repack", "launch_dequantize",
+    "launch_repack_128x32", "launch_inverse_repack_128x32", "launch_repack_mma_128x32",
     "launch_repack_mma_pair_128x32", "launch_repack_scales_128", "launch_repack_umma",
     "launch_inverse_repack_umma", "launch_final", "launch_final_fp32", "launch_gemm_variant",
-    "shard_range", "device_status", "selftest_wait_timeout", "QuantizedLinear",
-    "VARIANT_AUTO", "VARIANT_TC", "VARIANT_DECODE", "LIB_PATH",
+    "gemm_workspace_size", "launch_final_ws", "launch_final_fp32_ws", "workspace_for",
+    "launch_final_to_peers", "ipc_handle", "ipc_open", "ipc_close", "peer_barrier",
+    "shard_range", "device_status", "selftest_wait_timeout", "plan", "set_decode_schedule",
+    "QuantizedLinear", "VARIANT_AUTO", "VARIANT_TC", "VARIANT_DECODE", "DECODE_SCHEDULES",
+    "PLAN_KERNELS", "PLAN_SCHEDULES", "LIB_PATH",
 ]
 
 HERE = os.path.dirname(os.path.abspath(__file__))
