@@ -181,13 +181,18 @@ int i4g_gemm_fp32_ws(const void* A, const uint8_t* tiles, const void* scales,
 /* i4g_gemm_ws for callers that cannot allocate device memory or own a
  * workspace (e.g. a host framework whose memory is fully pooled, or a plugin
  * given only A, B and C): the split-K workspace is a fixed 40 MiB array in
- * static device memory, one per device, so nothing is allocated per call.
- * Limit: shapes whose split-K workspace exceeds 40 MiB are rejected with
- * I4G_ERR_SHAPE (none on a device with up to 160 SMs; B200 has 148).
+ * static device memory, one per device that loads the library, held until
+ * the process exits; nothing is allocated per call.
+ * Limit: a tcgen05 plan needs at most (2 * SMs - 2) x 128 KiB + 4 KiB, which
+ * fits for up to 160 SMs (B200 has 148); a larger need is rejected with
+ * I4G_ERR_SHAPE. A decode shape (M <= 16) whose stream-K workspace would not
+ * fit runs the decode kernel's cluster schedule, which needs none.
  * Set-up: the first call on a device loads the scratch and looks up its
  * address with that device current; make that call before any stream
- * capture. Each call clears the scratch's 1 KiB of arrival counters on
- * `stream` before its launch (they must start at zero).
+ * capture. The address is kept for the life of the process, so the entry
+ * point is not for use across a cudaDeviceReset. Each call clears the
+ * scratch's 4 KiB of arrival counters on `stream` before its launch (they
+ * must start at zero).
  * Calls on one device share the scratch: calls that overlap in time (e.g. on
  * two streams without ordering between them) race and give wrong results. */
 int i4g_gemm_static_scratch(const void* A, const uint8_t* tiles,
@@ -257,6 +262,36 @@ enum {
 int i4g_plan(int M, int N, int K, int group, int fp32_out, int sm_count,
              size_t workspace_bytes, int* kernel, int* schedule, int* param,
              size_t* bytes);
+
+/* ---- kernel registry queries (include/kernels.cuh:6-22, 85-105) ---------- */
+
+/* What the reference's KernelMetadata (kernels.cuh:6-14) and KernelResources
+ * (kernels.cuh:16-22) describe, for one instance of this library's kernels:
+ * variant I4G_VARIANT_TC with rows = 128 or 256 (activation rows per tile),
+ * or I4G_VARIANT_DECODE with rows = 8 (M <= 8) or 16 (M <= 16); group 32, 64
+ * or 128. int4gemm.hpp builds kernel_registry() / query_resources() on these.
+ * i4g_kernel_config is static (no device); i4g_kernel_resources asks the
+ * current device (cudaFuncGetAttributes and the occupancy calculator), as
+ * the reference's query_*_resources do. */
+typedef struct {
+  int rows;               /* activation rows per tile (the reference's BM) */
+  int cols;               /* weight columns per tile (BN) */
+  int bk;                 /* k per pipeline stage (BK) */
+  int mma_m, mma_n;       /* tensor-core instruction: weight columns x rows */
+  int stages;             /* activation pipeline stages */
+  int threads;            /* threads per CTA */
+  int dynamic_smem_bytes; /* dynamic shared memory per CTA */
+} i4g_kernel_config_t;
+
+typedef struct {
+  int registers_per_thread;
+  int static_smem_bytes;
+  int max_threads_per_block;
+  int active_blocks_per_sm;
+} i4g_kernel_resources_t;
+
+int i4g_kernel_config(int variant, int rows, int group, i4g_kernel_config_t* out);
+int i4g_kernel_resources(int variant, int rows, int group, i4g_kernel_resources_t* out);
 
 /* ---- decode schedule (no counterpart in the reference) --------------------- */
 

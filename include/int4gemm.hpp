@@ -16,6 +16,8 @@
 #include <cstdint>
 #include <stdexcept>
 #include <string>
+#include <utility>
+#include <vector>
 
 #include "i4g.h"
 
@@ -29,6 +31,26 @@ inline void i4g_throw_if(int status, const char* what) {
 
 using KernelLaunch = void (*)(const half*, const uint8_t*, const half*, half*, int, int, int,
                               int, cudaStream_t);
+
+// The reference's registry types (include/kernels.cuh:6-22): same members, so
+// that its harness (src/main.cu) fills its CSV rows from them unchanged.
+struct KernelMetadata {
+  const char* version;
+  const char* description;
+  int BM, BN, BK;
+  int warp_m, warp_n;
+  int stages;
+  int threads;
+  int smem_bytes;
+};
+
+struct KernelResources {
+  int registers_per_thread = -1;
+  int static_smem_bytes = -1;
+  int max_threads_per_block = -1;
+  int active_blocks_per_sm = -1;
+  float occupancy = -1.0f;
+};
 
 inline void launch_quantize(const half* b, uint8_t* packed, half* scales, int K, int N,
                             int group_size, cudaStream_t stream = nullptr) {
@@ -110,6 +132,45 @@ inline void launch_final(const half* a, const uint8_t* b, const half* s, half* c
 inline void launch_final_fp32(const half* a, const uint8_t* b, const half* s, float* c, int M,
                               int N, int K, int group, cudaStream_t stream) {
   i4g_throw_if(i4g_gemm_fp32(a, b, s, c, M, N, K, group, stream), "launch_final_fp32");
+}
+
+// kernel_registry() (kernels.cuh:83, gemm_final.cu): the reference lists its
+// twenty-odd experiment kernels and "final"; this library has one production
+// entry point, so the registry holds "final" alone. Its metadata is the
+// tcgen05 kernel's main instance (256 activation rows x 128 weight columns x
+// 64 k per stage; warp_m x warp_n carry the tensor-core instruction shape,
+// 128 weight columns x 256 rows, since no warp owns an output tile here).
+// launch_final runs the decode kernel for M <= 16.
+inline std::vector<std::pair<KernelMetadata, KernelLaunch>> kernel_registry() {
+  i4g_kernel_config_t c{};
+  i4g_throw_if(i4g_kernel_config(I4G_VARIANT_TC, 256, 128, &c), "kernel_registry");
+  KernelMetadata final_md{"final",
+                          "sm_100a tcgen05/TMEM fused W4A16: weights dequantised into TMEM, "
+                          "TMA activations, warp-specialised; decode kernel for M <= 16",
+                          c.rows, c.cols, c.bk, c.mma_m, c.mma_n, c.stages, c.threads,
+                          c.dynamic_smem_bytes};
+  return {{final_md, &launch_final}};
+}
+
+// query_final_resources (gemm_final.cu) / query_resources (kernels.cuh:105):
+// registers, static shared memory, the block limit and resident CTAs per SM
+// of the instance "final" runs for 4096-row problems (the reference's
+// harness computes occupancy from these, src/main.cu:376-377).
+inline KernelResources query_final_resources(int group) {
+  i4g_kernel_resources_t r{};
+  i4g_throw_if(i4g_kernel_resources(I4G_VARIANT_TC, 256, group, &r), "query_final_resources");
+  KernelResources out;
+  out.registers_per_thread = r.registers_per_thread;
+  out.static_smem_bytes = r.static_smem_bytes;
+  out.max_threads_per_block = r.max_threads_per_block;
+  out.active_blocks_per_sm = r.active_blocks_per_sm;
+  return out;
+}
+
+inline KernelResources query_resources(const std::string& version, int group) {
+  if (version != "final")
+    throw std::runtime_error("query_resources: no kernel \"" + version + "\" in this library");
+  return query_final_resources(group);
 }
 
 }  // namespace int4gemm

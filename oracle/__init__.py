@@ -44,16 +44,20 @@ class ErrorMetrics(ctypes.Structure):
                 ("rmse", ctypes.c_double), ("relative_l2", ctypes.c_double)]
 
 
-def build(ref: bool | None = None) -> None:
-    """Compile liboracle.so (and the reference checker when REF exists)."""
+def build(ref_path: str | None = None) -> None:
+    """Compile liboracle.so, and the reference checker (oracle/_ref) from the
+    reference checkout at `ref_path` (default: the I4G_REFERENCE environment
+    variable) when one is given and present."""
     subprocess.run(["make", "-C", HERE, "all"], check=True,
                    stdout=subprocess.DEVNULL)
-    ref_src = os.environ.get("I4G_REFERENCE", "/root/reference")
-    if ref is None:
-        ref = os.path.isfile(os.path.join(ref_src, "src", "reference.cu"))
-    if ref:
+    ref_src = ref_path or os.environ.get("I4G_REFERENCE")
+    if ref_src and os.path.isfile(os.path.join(ref_src, "src", "reference.cu")):
         subprocess.run(["make", "-C", HERE, "ref", f"REF={ref_src}"], check=True,
                        stdout=subprocess.DEVNULL)
+        # the reference's harness on this library (needs libi4g.so built)
+        if os.path.exists(os.path.join(os.path.dirname(HERE), "sm_120__gemm_b200", "libi4g.so")):
+            subprocess.run(["make", "-C", HERE, "harness", f"REF={ref_src}"], check=True,
+                           stdout=subprocess.DEVNULL)
 
 
 def lib():
@@ -61,7 +65,7 @@ def lib():
     with _lock:
         if _lib is None:
             if not os.path.exists(_LIB):
-                build(ref=False)
+                build()
             L = ctypes.CDLL(_LIB)
             L.i4o_h2f.restype = ctypes.c_float
             L.i4o_h2f.argtypes = [ctypes.c_uint16]
@@ -75,6 +79,11 @@ def lib():
             L.i4o_dequantize.argtypes = [_u8p, _u16p, _u16p, _i, _i, _i]
             L.i4o_gemm_rows.argtypes = [_u16p, _u16p, _f32p, _i, _i, _i, _i, _i]
             L.i4o_gemm_rows_fb.argtypes = [_u16p, _f32p, _f32p, _i, _i, _i, _i, _i]
+            L.i4o_gemm_rows_fb_noise.argtypes = [_u16p, _f32p, _f32p,
+                                                 ctypes.POINTER(ctypes.c_double),
+                                                 _i, _i, _i, _i, _i]
+            L.i4o_gemm_rows_f64.argtypes = [_u16p, _f32p, ctypes.POINTER(ctypes.c_double),
+                                            _i, _i, _i, _i, _i]
             L.i4o_abs_gemm_rows.argtypes = [_u16p, _u16p, _f32p, _i, _i, _i, _i, _i]
             L.i4o_compare_half.restype = ErrorMetrics
             L.i4o_compare_half.argtypes = [_u16p, _u16p, ctypes.c_size_t]
@@ -188,15 +197,30 @@ def dequantize(packed, scales, K: int, N: int, group: int) -> np.ndarray:
     return out
 
 
-def gemm_rows(a, b16, M: int, N: int, K: int, rows=None, threads: int = 1) -> np.ndarray:
+def widen(b16) -> np.ndarray:
+    """FP16 bit patterns -> flat binary32 array (exact), for reuse across calls."""
+    return h2f(_u16(b16)).reshape(-1)
+
+
+def _rows_parallel(fn, n_rows, threads):
+    if threads <= 1 or n_rows <= 1:
+        fn(0, n_rows)
+        return
+    chunks = np.array_split(np.arange(n_rows), threads)
+    with ThreadPoolExecutor(threads) as ex:
+        list(ex.map(lambda c: fn(int(c[0]), int(c[-1]) + 1) if len(c) else None, chunks))
+
+
+def gemm_rows(a, b16, M: int, N: int, K: int, rows=None, threads: int = 1,
+              bf=None) -> np.ndarray:
     """cpu_gemm_fp32 (src/reference.cu:55-64) on the given A rows: fp32 [len(rows), N].
 
     ``rows`` is a range/array of row indices (default: all). Rows are
-    independent, so they are split over ``threads`` host threads.
+    independent, so they are split over ``threads`` host threads. ``bf`` is
+    ``widen(b16)`` when the caller already has it.
     """
     a = _u16(a)
-    b16 = _u16(b16)
-    bf = h2f(b16).reshape(-1)
+    bf = widen(b16) if bf is None else bf
     idx = np.arange(M) if rows is None else np.asarray(rows)
     out = np.empty((len(idx), N), np.float32)
     L = lib()
@@ -206,13 +230,56 @@ def gemm_rows(a, b16, M: int, N: int, K: int, rows=None, threads: int = 1) -> np
             L.i4o_gemm_rows_fb(_p(a, _u16p), _p(bf, _f32p),
                                out[j].ctypes.data_as(_f32p), M, N, K, int(idx[j]), 1)
 
-    if threads <= 1 or len(idx) <= 1:
-        run(0, len(idx))
-    else:
-        chunks = np.array_split(np.arange(len(idx)), threads)
-        with ThreadPoolExecutor(threads) as ex:
-            list(ex.map(lambda c: run(int(c[0]), int(c[-1]) + 1) if len(c) else None, chunks))
+    _rows_parallel(run, len(idx), threads)
     return out
+
+
+def gemm_rows_noise(a, b16, M: int, N: int, K: int, rows=None, threads: int = 1, bf=None):
+    """cpu_gemm_fp32 on the given rows (as gemm_rows) and, per output, the
+    FP32 summation-noise scale 2^-24 * sqrt(sum_k p_k^2) of its running
+    partial sums p_k: (fp32 [rows, N], float64 [rows, N])."""
+    a = _u16(a)
+    bf = widen(b16) if bf is None else bf
+    idx = np.arange(M) if rows is None else np.asarray(rows)
+    out = np.empty((len(idx), N), np.float32)
+    p2 = np.empty((len(idx), N), np.float64)
+    L = lib()
+    dp = ctypes.POINTER(ctypes.c_double)
+
+    def run(lo, hi):
+        for j in range(lo, hi):
+            L.i4o_gemm_rows_fb_noise(_p(a, _u16p), _p(bf, _f32p), out[j].ctypes.data_as(_f32p),
+                                     p2[j].ctypes.data_as(dp), M, N, K, int(idx[j]), 1)
+
+    _rows_parallel(run, len(idx), threads)
+    return out, 2.0**-24 * np.sqrt(p2)
+
+
+def gemm_rows_f64(a, b16, M: int, N: int, K: int, rows=None, threads: int = 1,
+                  bf=None) -> np.ndarray:
+    """The exact result of the same operands for the given A rows: FP16 x FP16
+    products (exact in binary64) summed in binary64, float64 [len(rows), N].
+    Rounded once to FP16 (``f64_to_h``) it is the best FP16 answer, the anchor
+    the GEMM parity gate measures both this library and the reference from."""
+    a = _u16(a)
+    bf = widen(b16) if bf is None else bf
+    idx = np.arange(M) if rows is None else np.asarray(rows)
+    out = np.empty((len(idx), N), np.float64)
+    L = lib()
+    dp = ctypes.POINTER(ctypes.c_double)
+
+    def run(lo, hi):
+        for j in range(lo, hi):
+            L.i4o_gemm_rows_f64(_p(a, _u16p), _p(bf, _f32p), out[j].ctypes.data_as(dp),
+                                M, N, K, int(idx[j]), 1)
+
+    _rows_parallel(run, len(idx), threads)
+    return out
+
+
+def f64_to_h(x) -> np.ndarray:
+    """binary64 -> FP16 bit patterns, rounded once to nearest even."""
+    return np.ascontiguousarray(np.asarray(x, np.float64).astype(np.float16)).view(np.uint16)
 
 
 def abs_gemm_rows(a, b16, M: int, N: int, K: int, rows=None) -> np.ndarray:

@@ -136,6 +136,43 @@ void i4o_gemm_rows_fb(const uint16_t* a, const float* bf, float* c,
   }
 }
 
+void i4o_gemm_rows_fb_noise(const uint16_t* a, const float* bf, float* c, double* p2,
+                            int M, int N, int K, int row0, int rows) {
+  (void)M;
+  for (int r = 0; r < rows; ++r) {
+    float* crow = c + (size_t)r * N;
+    double* prow = p2 + (size_t)r * N;
+    for (int n = 0; n < N; ++n) {
+      crow[n] = 0.0f;
+      prow[n] = 0.0;
+    }
+    const uint16_t* arow = a + (size_t)(row0 + r) * K;
+    for (int k = 0; k < K; ++k) {
+      const float av = i4o_h2f(arow[k]);
+      const float* brow = bf + (size_t)k * N;
+      for (int n = 0; n < N; ++n) {
+        crow[n] += av * brow[n];
+        prow[n] += (double)crow[n] * (double)crow[n];
+      }
+    }
+  }
+}
+
+void i4o_gemm_rows_f64(const uint16_t* a, const float* bf, double* c,
+                       int M, int N, int K, int row0, int rows) {
+  (void)M;
+  for (int r = 0; r < rows; ++r) {
+    double* crow = c + (size_t)r * N;
+    for (int n = 0; n < N; ++n) crow[n] = 0.0;
+    const uint16_t* arow = a + (size_t)(row0 + r) * K;
+    for (int k = 0; k < K; ++k) {
+      const double av = (double)i4o_h2f(arow[k]);
+      const float* brow = bf + (size_t)k * N;
+      for (int n = 0; n < N; ++n) crow[n] += av * (double)brow[n];
+    }
+  }
+}
+
 void i4o_gemm_rows(const uint16_t* a, const uint16_t* b, float* c,
                    int M, int N, int K, int row0, int rows) {
   /* B is widened to binary32 once (exact); the arithmetic is the reference

@@ -71,6 +71,22 @@ void i4o_gemm_rows_fb(const uint16_t* a, const float* bf, float* c,
 void i4o_abs_gemm_rows(const uint16_t* a, const uint16_t* b, float* c,
                        int M, int N, int K, int row0, int rows);
 
+/* i4o_gemm_rows_fb that also returns, per output, the sum of the squares of
+ * the loop's own running FP32 partial sums p_k (k = 1..K), in binary64.
+ * 2^-24 * sqrt(sum p_k^2) is the scale of the rounding noise of FP32
+ * summation for that output: each add contributes an error of at most
+ * 2^-24 |p_k|, of either sign. */
+void i4o_gemm_rows_fb_noise(const uint16_t* a, const float* bf, float* c, double* p2,
+                            int M, int N, int K, int row0, int rows);
+
+/* The exact product of the same operands: each FP16 x FP16 product is exact
+ * in binary64 and the K products are summed in binary64 (k ascending), so
+ * for K <= 2^20 the result is within far less than an FP16 ulp of the exact
+ * sum. Rounded once to FP16 it is the best FP16 answer for each output: the
+ * anchor of the GEMM parity gate. bf is B widened to binary32 (exact). */
+void i4o_gemm_rows_f64(const uint16_t* a, const float* bf, double* c,
+                       int M, int N, int K, int row0, int rows);
+
 /* src/reference.cu:39-53 */
 i4o_error_metrics i4o_compare_half(const uint16_t* got, const uint16_t* ref,
                                    size_t count);

@@ -29,6 +29,7 @@ __all__ = [
     "gemm_workspace_size", "launch_final_ws", "launch_final_fp32_ws", "workspace_for",
     "launch_final_to_peers", "ipc_handle", "ipc_open", "ipc_close", "peer_barrier",
     "shard_range", "device_status", "selftest_wait_timeout", "plan", "set_decode_schedule",
+    "kernel_config", "kernel_resources",
     "QuantizedLinear", "VARIANT_AUTO", "VARIANT_TC", "VARIANT_DECODE", "DECODE_SCHEDULES",
     "PLAN_KERNELS", "PLAN_SCHEDULES", "LIB_PATH",
 ]
@@ -85,6 +86,20 @@ _SIGNATURES = {
                          _vp],
     "i4g_layout_version": [],
 }
+
+
+class _KernelConfig(ctypes.Structure):
+    _fields_ = [(n, _i) for n in ("rows", "cols", "bk", "mma_m", "mma_n", "stages", "threads",
+                                  "dynamic_smem_bytes")]
+
+
+class _KernelResources(ctypes.Structure):
+    _fields_ = [(n, _i) for n in ("registers_per_thread", "static_smem_bytes",
+                                  "max_threads_per_block", "active_blocks_per_sm")]
+
+
+_SIGNATURES["i4g_kernel_config"] = [_i, _i, _i, ctypes.POINTER(_KernelConfig)]
+_SIGNATURES["i4g_kernel_resources"] = [_i, _i, _i, ctypes.POINTER(_KernelResources)]
 
 
 def load() -> ctypes.CDLL:
@@ -339,6 +354,23 @@ def plan(M: int, N: int, K: int, group: int, sm_count: int, workspace_bytes: int
           ctypes.byref(s), ctypes.byref(p), ctypes.byref(b))
     return {"kernel": PLAN_KERNELS[k.value], "schedule": PLAN_SCHEDULES[s.value],
             "param": p.value, "workspace_bytes": b.value}
+
+
+def kernel_config(variant: int, rows: int, group: int) -> dict:
+    """C ABI i4g_kernel_config (the reference's KernelMetadata, kernels.cuh:6-14):
+    tile, stages, threads and shared memory of one kernel instance; no device."""
+    c = _KernelConfig()
+    _call("i4g_kernel_config", variant, rows, group, ctypes.byref(c))
+    return {n: getattr(c, n) for n, _ in _KernelConfig._fields_}
+
+
+def kernel_resources(variant: int, rows: int, group: int) -> dict:
+    """C ABI i4g_kernel_resources (the reference's KernelResources,
+    kernels.cuh:16-22): registers, static shared memory, block limit and
+    resident CTAs per SM of one kernel instance on the current device."""
+    r = _KernelResources()
+    _call("i4g_kernel_resources", variant, rows, group, ctypes.byref(r))
+    return {n: getattr(r, n) for n, _ in _KernelResources._fields_}
 
 
 DECODE_SCHEDULES = {"auto": 0, "cluster": 1, "streamk": 2}

@@ -588,9 +588,7 @@ int i4g_gemm_static_scratch(const void* A, const uint8_t* tiles, const void* sca
   }
   void* scratch = nullptr;
   if (need > 0) {
-    int ordinal = -1;
-    cudaError_t e = cudaGetDevice(&ordinal);
-    if (e == cudaSuccess) e = i4g::static_scratch(ordinal, &scratch);
+    cudaError_t e = i4g::static_scratch(&scratch);
     if (e != cudaSuccess) return record_cuda(e, "cudaGetSymbolAddress(static scratch)");
     // The arrival counters must be zero when the kernel starts. Completed
     // launches leave them so; clearing them here keeps a launch that gave up
@@ -730,6 +728,41 @@ int i4g_plan(int M, int N, int K, int group, int fp32_out, int sm_count,
     *schedule = I4G_PLAN_WHOLE;
     *param = plan.grid;
   }
+  return I4G_OK;
+}
+
+static int kernel_instance(int variant, int rows, int group) {
+  int st = check_group(group, group, false);
+  if (st != I4G_OK) return st;
+  if (variant == I4G_VARIANT_TC && (rows == 128 || rows == 256)) return I4G_OK;
+  if (variant == I4G_VARIANT_DECODE && (rows == 8 || rows == 16)) return I4G_OK;
+  return fail(I4G_ERR_VARIANT, "no kernel instance for variant %d with %d rows", variant, rows);
+}
+
+int i4g_kernel_config(int variant, int rows, int group, i4g_kernel_config_t* out) {
+  if (!out) return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
+  int st = kernel_instance(variant, rows, group);
+  if (st != I4G_OK) return st;
+  i4g::KernelConfig c{};
+  const bool ok = variant == I4G_VARIANT_TC ? i4g::tc::config(rows, group, &c)
+                                            : i4g::dec::config(rows, group, &c);
+  if (!ok) return fail(I4G_ERR_VARIANT, "no kernel instance for %d rows", rows);
+  *out = i4g_kernel_config_t{c.rows, c.cols, c.bk, c.mma_m, c.mma_n, c.stages, c.threads,
+                             c.dynamic_smem};
+  return I4G_OK;
+}
+
+int i4g_kernel_resources(int variant, int rows, int group, i4g_kernel_resources_t* out) {
+  if (!out) return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
+  int st = kernel_instance(variant, rows, group);
+  if (st != I4G_OK) return st;
+  DeviceInfo* dev = nullptr;
+  if ((st = current_device(&dev)) != I4G_OK) return st;
+  i4g::KernelResources r{};
+  const cudaError_t e = variant == I4G_VARIANT_TC ? i4g::tc::resources(rows, group, &r)
+                                                  : i4g::dec::resources(rows, group, &r);
+  if (e != cudaSuccess) return record_cuda(e, "kernel attribute query");
+  *out = i4g_kernel_resources_t{r.registers, r.static_smem, r.max_threads, r.active_per_sm};
   return I4G_OK;
 }
 

@@ -836,6 +836,48 @@ cudaError_t launch_mt(const CUtensorMap& act_map, const uint8_t* tiles, const __
   return cudaErrorInvalidValue;
 }
 
+template <int MT, int GROUP>
+KernelConfig config_of() {
+  constexpr int S = stages_for<MT, GROUP>();
+  return KernelConfig{MT * 8, NCOL, KPS * BK, 16, MT * 8, S, THREADS, Layout<MT, GROUP, S>::DYN};
+}
+
+template <int MT, int GROUP>
+cudaError_t resources_of(KernelResources* out) {
+  constexpr int S = stages_for<MT, GROUP>();
+  using L = Layout<MT, GROUP, S>;
+  auto kernel = decode_kernel<MT, GROUP, S>;
+  static std::atomic<uint64_t> configured{0};
+  cudaError_t e = ensure_dynamic_smem(kernel, L::DYN, configured);
+  if (e != cudaSuccess) return e;
+  cudaFuncAttributes a{};
+  if ((e = cudaFuncGetAttributes(&a, kernel)) != cudaSuccess) return e;
+  int active = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&active, kernel, THREADS, L::DYN);
+  if (e != cudaSuccess) return e;
+  *out = KernelResources{a.numRegs, static_cast<int>(a.sharedSizeBytes), a.maxThreadsPerBlock,
+                         active};
+  return cudaSuccess;
+}
+
+bool config(int rows, int group, KernelConfig* out) {
+#define I4G_DEC_CFG(R, G) \
+  if (rows == R * 8 && group == G) { *out = config_of<R, G>(); return true; }
+  I4G_DEC_CFG(1, 32) I4G_DEC_CFG(1, 64) I4G_DEC_CFG(1, 128)
+  I4G_DEC_CFG(2, 32) I4G_DEC_CFG(2, 64) I4G_DEC_CFG(2, 128)
+#undef I4G_DEC_CFG
+  return false;
+}
+
+cudaError_t resources(int rows, int group, KernelResources* out) {
+#define I4G_DEC_RES(R, G) \
+  if (rows == R * 8 && group == G) return resources_of<R, G>(out);
+  I4G_DEC_RES(1, 32) I4G_DEC_RES(1, 64) I4G_DEC_RES(1, 128)
+  I4G_DEC_RES(2, 32) I4G_DEC_RES(2, 64) I4G_DEC_RES(2, 128)
+#undef I4G_DEC_RES
+  return cudaErrorInvalidValue;
+}
+
 int rows_for(int M) { return M <= 8 ? 8 : 16; }
 
 bool supported(int M, int K, int group) {

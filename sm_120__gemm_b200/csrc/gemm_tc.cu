@@ -772,6 +772,47 @@ cudaError_t launch_group(const CUtensorMap& act_map, const uint8_t* tiles,
   }
 }
 
+template <int TILE_M, int GROUP>
+KernelConfig config_of() {
+  using L = Cfg<TILE_M>;
+  return KernelConfig{TILE_M, TILE_N, BK, TILE_N, TILE_M, L::A_STAGES, THREADS, L::DYN_BYTES};
+}
+
+template <int TILE_M, int GROUP>
+cudaError_t resources_of(KernelResources* out) {
+  auto kernel = gemm_tc_kernel<TILE_M, GROUP, kOutHalf>;
+  static std::atomic<uint64_t> configured{0};
+  cudaError_t e = ensure_dynamic_smem(kernel, Cfg<TILE_M>::DYN_BYTES, configured);
+  if (e != cudaSuccess) return e;
+  cudaFuncAttributes a{};
+  if ((e = cudaFuncGetAttributes(&a, kernel)) != cudaSuccess) return e;
+  int active = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&active, kernel, THREADS,
+                                                    Cfg<TILE_M>::DYN_BYTES);
+  if (e != cudaSuccess) return e;
+  *out = KernelResources{a.numRegs, static_cast<int>(a.sharedSizeBytes), a.maxThreadsPerBlock,
+                         active};
+  return cudaSuccess;
+}
+
+bool config(int tile_m, int group, KernelConfig* out) {
+#define I4G_TC_CFG(TM, G) \
+  if (tile_m == TM && group == G) { *out = config_of<TM, G>(); return true; }
+  I4G_TC_CFG(128, 32) I4G_TC_CFG(128, 64) I4G_TC_CFG(128, 128)
+  I4G_TC_CFG(256, 32) I4G_TC_CFG(256, 64) I4G_TC_CFG(256, 128)
+#undef I4G_TC_CFG
+  return false;
+}
+
+cudaError_t resources(int tile_m, int group, KernelResources* out) {
+#define I4G_TC_RES(TM, G) \
+  if (tile_m == TM && group == G) return resources_of<TM, G>(out);
+  I4G_TC_RES(128, 32) I4G_TC_RES(128, 64) I4G_TC_RES(128, 128)
+  I4G_TC_RES(256, 32) I4G_TC_RES(256, 64) I4G_TC_RES(256, 128)
+#undef I4G_TC_RES
+  return cudaErrorInvalidValue;
+}
+
 int choose_tile_m(int M, int N, int sm_count) {
   // A 128 x N x 16 MMA costs about the same for any N <= 256, so N = 256
   // wins unless the activation rows (M) do not fill it.

@@ -38,6 +38,17 @@ struct Outputs {
   int col0;
 };
 
+// Static configuration and device resources of one kernel instance, for the
+// registry queries of the C ABI (i4g_kernel_config / i4g_kernel_resources).
+struct KernelConfig {
+  int rows, cols, bk;        // activation rows, weight columns, k per stage
+  int mma_m, mma_n;          // tensor-core instruction shape (weights x rows)
+  int stages, threads, dynamic_smem;
+};
+struct KernelResources {
+  int registers, static_smem, max_threads, active_per_sm;
+};
+
 namespace tc {
 // Arrival counters (tickets) at the start of a split-K workspace, then the
 // FP32 partials; the decode kernel's stream-K schedule uses the same layout.
@@ -63,6 +74,10 @@ Plan make_plan(int tile_m, int M, int N, int K, int sm_count, size_t budget,
 
 // TILE_M (activation rows per tile, the MMA-N) for a problem on sm_count SMs.
 int choose_tile_m(int M, int N, int sm_count);
+// The FP16-C instance for tile_m (128 or 256) and group (32, 64, 128);
+// resources() needs a current device.
+bool config(int tile_m, int group, KernelConfig* out);
+cudaError_t resources(int tile_m, int group, KernelResources* out);
 cudaError_t launch(const CUtensorMap& act_map, int tile_m, const uint8_t* tiles,
                    const __half* scales, const Outputs& out, bool fp32_out, int M, int N, int K,
                    int group, const Plan& plan, void* workspace, int* status,
@@ -86,6 +101,9 @@ struct SkPlan {
 SkPlan sk_plan(int M, int N, int K, int sm_count);
 // Cluster size of the cluster schedule (K split of each column tile).
 int choose_cluster(int N, int K, int sm_count);
+// The cluster-schedule instance for rows (8: M <= 8, 16: M <= 16) and group.
+bool config(int rows, int group, KernelConfig* out);
+cudaError_t resources(int rows, int group, KernelResources* out);
 constexpr int kScheduleAuto = 0, kScheduleCluster = 1, kScheduleStreamK = 2;
 void set_schedule(int mode);
 // Launches the stream-K schedule when `workspace` holds sk_plan's bytes and
@@ -121,7 +139,8 @@ cudaError_t inverse_repack_umma(const uint8_t* tiles, uint8_t* packed, int K, in
                                 cudaStream_t stream);
 }  // namespace prep
 
-// Fixed-size split-K scratch in static device memory (static_scratch.cu).
+// Fixed-size split-K scratch in static device memory (static_scratch.cu):
+// its size, and its device address on the current device.
 size_t static_scratch_bytes();
-cudaError_t static_scratch(int device, void** out);
+cudaError_t static_scratch(void** out);
 }  // namespace i4g

@@ -28,6 +28,10 @@ class HostPipeline:
         self.d2h = torch.cuda.Stream(self.device)
         ev = lambda: [torch.cuda.Event() for _ in range(depth)]  # noqa: E731
         self.a_ready, self.a_free, self.c_done, self.c_free = ev(), ev(), ev(), ev()
+        # jobs enqueued over every run(): a slot is reused (and its events
+        # must be waited for) from the depth-th job of the pipeline's life on,
+        # whatever run() call it belongs to
+        self._jobs = 0
 
     def run(self, jobs, after: torch.cuda.Event | None = None) -> torch.cuda.Event:
         """Enqueue `jobs`, a list of (QuantizedLinear, A host [M, K] fp16, C
@@ -37,12 +41,14 @@ class HostPipeline:
         if after is not None:
             for s in streams:
                 s.wait_event(after)
-        for i, (lin, a_host, c_host) in enumerate(jobs):
-            slot = i % self.depth
+        for lin, a_host, c_host in jobs:
+            n = self._jobs
+            self._jobs += 1
+            slot = n % self.depth
             M, K = a_host.shape
             a = self.a_dev[slot][: M * K].view(M, K)
             c = self.c_dev[slot][: M * lin.N].view(M, lin.N)
-            reuse = i >= self.depth
+            reuse = n >= self.depth
             with torch.cuda.stream(self.h2d):
                 if reuse:
                     self.h2d.wait_event(self.a_free[slot])

@@ -45,34 +45,50 @@ def gather_columns(c_local: torch.Tensor, group=None, out: torch.Tensor | None =
 
 
 class PeerOutputs:
-    """Every rank's full C buffer ([max_m, N] FP16), mapped into every rank
+    """Every rank's full C buffers ([max_m, N] FP16), mapped into every rank
     (CUDA IPC, plain peer-to-peer mappings), so that one GEMM launch per rank
     can write its column block into all of them: the all-gather fused into
     the GEMM epilogue. The same allocation holds this rank's barrier flags
-    (one 64-bit flag per rank, after C), which the peers set through their
-    mappings (``i4g_peer_barrier``). Collective: every rank of `group`
-    constructs it."""
+    (one 64-bit flag per rank, after the C buffers), which the peers set
+    through their mappings (``i4g_peer_barrier``). Collective: every rank of
+    `group` constructs it, and every rank makes the same sequence of calls.
+
+    Reuse rule. After call i's barrier a rank reads its C while its peers go
+    on to call i+1, whose peer stores would overwrite C under the reader if
+    both calls used one buffer (write after read). With ``slots=2`` (the
+    default) consecutive calls alternate between two buffers: call i+2
+    reuses call i's buffer, and no rank starts call i+2 before every rank has
+    passed call i+1's barrier, which on each rank runs after everything that
+    rank enqueued before call i+1. So call i's C may be read by work enqueued
+    on the call's stream before the rank's call i+1. With ``slots=1`` each
+    call first runs a barrier that waits for every rank to reach the call,
+    i.e. to have finished reading the previous result (half the memory, one
+    more barrier per call)."""
 
     FLAG_BYTES = 256  # room for 32 ranks; the barrier kernel takes up to 8
 
-    def __init__(self, max_m: int, N: int, device, group=None):
-        self.max_m, self.N, self.group = max_m, N, group
+    def __init__(self, max_m: int, N: int, device, group=None, slots: int = 2):
+        if slots not in (1, 2):
+            raise ValueError("slots must be 1 or 2")
+        self.max_m, self.N, self.group, self.slots = max_m, N, group, slots
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         c_bytes = max_m * N * 2
-        self._flag_off = (c_bytes + 255) // 256 * 256
+        slot_bytes = (c_bytes + 255) // 256 * 256
+        self._flag_off = slots * slot_bytes
         self._raw = torch.empty(self._flag_off + self.FLAG_BYTES, dtype=torch.uint8,
                                 device=device)
         self._raw[self._flag_off:].zero_()
         # the flags are zero before any peer can reach them (the handle
         # exchange below is the first point at which a peer could)
         torch.cuda.synchronize(device)
-        self.buf = self._raw[:c_bytes].view(torch.float16)
+        self.bufs = [self._raw[i * slot_bytes: i * slot_bytes + c_bytes].view(torch.float16)
+                     for i in range(slots)]
         mine = ipc_handle(self._raw)
         handles = [None] * self.world
         dist.all_gather_object(handles, mine, group=group)
         self._opened = []
-        peers = []
+        peer_bases = []
         self._flag_ptrs = [0] * self.world
         for r in range(self.world):
             if r == self.rank:
@@ -81,14 +97,35 @@ class PeerOutputs:
             h, off = handles[r]
             base = ipc_open(h)
             self._opened.append(base)
-            peers.append(base + off)
+            peer_bases.append(base + off)
             self._flag_ptrs[r] = base + off + self._flag_off
-        # this GPU's copy first, then the peers' (the kernel writes them in order)
-        self.dsts = [self.buf.data_ptr()] + peers
+        # per slot: this GPU's copy first, then the peers' (the kernel writes
+        # them in order)
+        local = self._raw.data_ptr()
+        self.dsts_by_slot = [[local + i * slot_bytes] + [p + i * slot_bytes for p in peer_bases]
+                             for i in range(slots)]
         self._epoch = 0
+        self._calls = 0
 
-    def view(self, M: int) -> torch.Tensor:
-        return self.buf[: M * self.N].view(M, self.N)
+    @property
+    def dsts(self):
+        """Destination pointers of the buffer the next call writes."""
+        return self.dsts_by_slot[self._calls % self.slots]
+
+    def view(self, M: int, slot: int | None = None) -> torch.Tensor:
+        """[M, N] view of a buffer (default: the one the last call wrote)."""
+        if slot is None:
+            slot = (self._calls - 1) % self.slots
+        return self.bufs[slot][: M * self.N].view(M, self.N)
+
+    def begin_call(self, stream=None) -> list:
+        """Destinations of the next call; with one slot, first a barrier that
+        every rank's previous reads are ordered before."""
+        if self.slots == 1 and self._calls > 0:
+            self.barrier(stream)
+        dsts = self.dsts
+        self._calls += 1
+        return dsts
 
     def barrier(self, stream=None) -> None:
         """Stream-ordered cross-rank barrier (a flag per rank pair over the
@@ -133,14 +170,17 @@ class ColumnParallelLinear:
     def forward_to_peers(self, a: torch.Tensor, outs: PeerOutputs, stream=None) -> torch.Tensor:
         """The full C on every rank with no separate collective: this rank's
         GEMM stores its columns into every rank's buffer over NVLink, then a
-        barrier orders the readers. Returns this rank's [M, N] view."""
+        barrier orders the readers. Returns this rank's [M, N] view, readable
+        by work enqueued before this rank's next call (``PeerOutputs``'
+        reuse rule)."""
         a = a.contiguous()
         M = a.shape[0]
         if M > outs.max_m or outs.N != self.N:
             raise ValueError("PeerOutputs too small for this call")
         loc = self.local
         ws = workspace_for(M, loc.N, loc.K, a.device, stream)
-        launch_final_to_peers(a, loc.tiles, loc.scales, outs.dsts, self.N, self.n0, M, loc.N,
+        dsts = outs.begin_call(stream)
+        launch_final_to_peers(a, loc.tiles, loc.scales, dsts, self.N, self.n0, M, loc.N,
                               loc.K, loc.group, ws, stream)
         outs.barrier(stream)
         return outs.view(M)

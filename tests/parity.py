@@ -1,18 +1,48 @@
 """Shared helpers for the GPU parity tests (CPU-side checking only).
 
-Tolerance of the GEMM parity: each FP16 output is
-within 1 FP16 ulp of the reference's CPU path (dequantize_cpu + the
-sequential-k FP32 cpu_gemm_fp32, rounded to FP16), except where the two FP32
-summation orders themselves may differ by more than that: there the bound is
-1 ulp + gamma * sum_k |a_k * b_k| with gamma = 2 * K * 2^-24 (the standard
-worst-case bound for two different FP32 summation orders of K terms).
+GEMM parity gate (the north star's "max |err| <= 1 FP16 ulp of the
+reference's FP32-accumulated dequant-then-GEMM path"), anchored on the exact
+result. For every FP16 output, with
+  ref16   = half(cpu_gemm_fp32)   the reference's CPU path (src/reference.cu:55-64),
+  truth16 = half(exact sum)       the same FP16 products summed in binary64,
+the output passes when
+  (a) ulp(ours, ref16) <= 1, or
+  (b) ulp(ours, truth16) <= ulp(ref16, truth16) + 1,
+i.e. it is within one ulp of the reference's output, or no further from the
+exact answer than the reference's own sequential FP32 sum is, plus one ulp.
+
+(a) and (b) cannot both be required of a kernel that sums in another order:
+where the sum cancels to near zero, FP32 rounding noise exceeds the FP16
+resolution of the result and the reference's own path lands up to tens of
+ulps from the exact sum, at a point set by its particular order. There a
+kernel that is more accurate on average still lands further than the
+reference on some outputs by chance. So an output that meets neither passes
+only as
+  (c) |ours - exact| <= ulp(truth16) / 2 + KAPPA * sigma,
+where sigma = 2^-24 * sqrt(sum_k p_k^2) is the FP32 summation-noise scale of
+that output, computed from the reference loop's own running partial sums p_k.
+For an output of ordinary size sigma is far below an ulp, so (c) reduces to
+"correctly rounded"; it admits more only in the noise regime. The reports
+count the outputs passing by (c) and the largest |ours - exact| / sigma.
 """
 from __future__ import annotations
+
+from typing import NamedTuple
 
 import numpy as np
 import torch
 
 import oracle
+
+KAPPA = 8.0  # noise-regime allowance, in units of the FP32 noise scale sigma
+
+
+class Expected(NamedTuple):
+    """The oracle's answers for some rows of A."""
+    rows: np.ndarray
+    ref32: np.ndarray    # the reference's sequential FP32 path
+    truth64: np.ndarray  # the exact sum (binary64)
+    noise: np.ndarray    # sigma, the FP32 summation-noise scale of each output
 
 
 def make_inputs(M, N, K, seed_a=1234, seed_b=5678, a_dist="uniform", w_sigma=0.02):
@@ -32,49 +62,80 @@ def u16(t: torch.Tensor) -> np.ndarray:
     return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
 
 
-def fp16_spacing(x: np.ndarray) -> np.ndarray:
-    ax = np.abs(x.astype(np.float64))
-    e = np.floor(np.log2(np.maximum(ax, 2.0**-24)))
-    return np.where(ax < 2.0**-14, 2.0**-24, 2.0 ** (e - 10))
+def reference_rows(a16: np.ndarray, deq16: np.ndarray, M: int, N: int, K: int, rows,
+                   threads: int = 8) -> Expected:
+    """The oracle's answers (Expected) for the given rows of A."""
+    rows = np.arange(M) if rows is None else np.asarray(rows)
+    bf = oracle.widen(deq16)
+    ref32, noise = oracle.gemm_rows_noise(a16, None, M, N, K, rows=rows, threads=threads, bf=bf)
+    truth64 = oracle.gemm_rows_f64(a16, None, M, N, K, rows=rows, threads=threads, bf=bf)
+    return Expected(rows, ref32, truth64, noise)
 
 
-def gemm_report(got16: np.ndarray, ref32: np.ndarray, abs32: np.ndarray, K: int) -> dict:
-    """Check FP16 GEMM output against the FP32 oracle; returns stats and 'ok'."""
-    ref16 = oracle.f2h(ref32)
-    ulp = oracle.ulp_distance(got16, ref16)
-    got = oracle.h2f(got16).astype(np.float64)
-    ref = oracle.h2f(ref16).astype(np.float64)
-    gamma = 2.0 * K * 2.0**-24
-    bound = fp16_spacing(ref32) + gamma * abs32.astype(np.float64)
-    ok = (ulp <= 1) | (np.abs(got - ref) <= bound)
-    hist = {"0": int((ulp == 0).sum()), "1": int((ulp == 1).sum()),
-            "2": int((ulp == 2).sum()), ">2": int((ulp > 2).sum())}
+def oracle_case(a16: np.ndarray, w16: np.ndarray, M: int, N: int, K: int, group: int,
+                rows=None, threads: int = 8):
+    """quantize_cpu -> dequantize_cpu of W, then the oracle's answers for the
+    given rows of A (all rows by default): (Expected, deq16)."""
+    packed, scales = oracle.quantize(w16, K, N, group)
+    deq = oracle.dequantize(packed, scales, K, N, group)
+    return reference_rows(a16, deq, M, N, K, rows, threads), deq
+
+
+def fp16_ulp(h16: np.ndarray) -> np.ndarray:
+    """Spacing of FP16 at each value (2^-24 in the subnormal range)."""
+    ax = np.abs(oracle.h2f(h16).astype(np.float64))
+    e = np.floor(np.log2(np.maximum(ax, 2.0**-14)))
+    return 2.0 ** (e - 10)
+
+
+def gemm_report(got16: np.ndarray, exp: Expected) -> dict:
+    """The gate of the module docstring on FP16 outputs; returns stats and 'ok'."""
+    ref16 = oracle.f2h(exp.ref32)
+    truth16 = oracle.f64_to_h(exp.truth64)
+    d_ref = oracle.ulp_distance(got16, ref16)
+    d_ours = oracle.ulp_distance(got16, truth16)
+    d_refpath = oracle.ulp_distance(ref16, truth16)
+    a_ok = d_ref <= 1
+    b_ok = d_ours <= d_refpath + 1
+    err = np.abs(oracle.h2f(got16).astype(np.float64) - exp.truth64)
+    c_ok = err <= 0.5 * fp16_ulp(truth16) + KAPPA * exp.noise
+    ok = a_ok | b_ok | c_ok
+    by_c = ~(a_ok | b_ok) & c_ok
+    hist = {"0": int((d_ref == 0).sum()), "1": int((d_ref == 1).sum()),
+            "2": int((d_ref == 2).sum()), ">2": int((d_ref > 2).sum())}
     m = oracle.compare_half(got16, ref16)
-    return {"ok": bool(ok.all()), "bad": int((~ok).sum()), "ulp_hist": hist,
-            "max_ulp": int(ulp.max()), "max_abs": m.max_abs, "rel_l2": m.relative_l2}
+    ratio = np.where(~(a_ok | b_ok), err / np.maximum(exp.noise, 1e-300), 0.0)
+    return {"ok": bool(ok.all()), "bad": int((~ok).sum()), "outputs": int(d_ref.size),
+            "ulp_hist": hist, "max_ulp": int(d_ref.max()),
+            "above_1ulp": int((d_ref > 1).sum()),
+            "passed_by_noise_rule": int(by_c.sum()),
+            "max_err_over_sigma": round(float(ratio.max()), 3),
+            "max_ulp_vs_exact_ours": int(d_ours.max()),
+            "max_ulp_vs_exact_ref": int(d_refpath.max()),
+            "closer_to_exact_ours": int((d_ours < d_refpath).sum()),
+            "closer_to_exact_ref": int((d_refpath < d_ours).sum()),
+            "max_abs": m.max_abs, "rel_l2": m.relative_l2}
 
 
-def fp32_report(got32: np.ndarray, ref32: np.ndarray, abs32: np.ndarray, K: int) -> dict:
-    gamma = 2.0 * K * 2.0**-24
-    diff = np.abs(got32.astype(np.float64) - ref32.astype(np.float64))
-    bound = gamma * abs32.astype(np.float64) + 1e-30
-    return {"ok": bool((diff <= bound).all()), "max_abs": float(diff.max()),
-            "max_rel_to_bound": float((diff / bound).max())}
+def assert_gemm_parity(rep: dict) -> None:
+    """Every output passes (a), (b) or (c); outputs more than an ulp from the
+    reference's path, and outputs that need (c), are rare."""
+    assert rep["ok"], rep
+    assert rep["above_1ulp"] <= max(8, rep["outputs"] // 200), rep
+    assert rep["passed_by_noise_rule"] <= max(8, rep["outputs"] // 1000), rep
 
 
-def fp64_attribution(a16_rows: np.ndarray, deq16: np.ndarray, got16: np.ndarray,
-                     ref32: np.ndarray) -> dict:
-    """Attribute the residual against an FP64 oracle: the dequantized FP16
-    products (exact in FP64) summed in FP64 and rounded once to FP16 give the
-    best FP16 answer for each output; this output and the reference's FP32
-    path (rounded to FP16) are both measured from it in ulps. Where the two
-    differ by more than an ulp, this says which one the summation order put
-    further from the exact product."""
-    a = oracle.h2f(a16_rows).astype(np.float64)
-    w = oracle.h2f(deq16).astype(np.float64)
-    truth16 = (a @ w).astype(np.float16).view(np.uint16)
-    ours = oracle.ulp_distance(got16, truth16)
-    ref = oracle.ulp_distance(oracle.f2h(ref32), truth16)
-    return {"fp64_max_ulp_ours": int(ours.max()), "fp64_max_ulp_ref": int(ref.max()),
-            "fp64_outputs_closer_ours": int((ours < ref).sum()),
-            "fp64_outputs_closer_ref": int((ref < ours).sum())}
+def fp32_report(got32: np.ndarray, exp: Expected) -> dict:
+    """FP32 C: no further from the exact sum than the reference's FP32 path is
+    plus KAPPA * sigma (the FP32 summation-noise scale of the output)."""
+    got = got32.astype(np.float64)
+    err = np.abs(got - exp.truth64)
+    ref_err = np.abs(exp.ref32.astype(np.float64) - exp.truth64)
+    bound = ref_err + KAPPA * exp.noise + 1e-45
+    return {"ok": bool((err <= bound).all()),
+            "max_abs_vs_ref": float(np.abs(got - exp.ref32.astype(np.float64)).max()),
+            "max_abs_vs_exact_ours": float(err.max()),
+            "max_abs_vs_exact_ref": float(ref_err.max()),
+            "max_err_over_sigma": round(float((err / np.maximum(exp.noise, 1e-300)).max()), 3),
+            "closer_to_exact_ours": int((err < ref_err).sum()),
+            "closer_to_exact_ref": int((ref_err < err).sum())}

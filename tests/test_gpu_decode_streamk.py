@@ -12,7 +12,7 @@ import pytest
 import torch
 
 import oracle
-from parity import gemm_report, make_inputs, u16
+from parity import assert_gemm_parity, gemm_report, make_inputs, oracle_case, u16
 from plans import TICKET_BYTES, expected_decode_plan
 
 pytestmark = pytest.mark.gpu
@@ -34,7 +34,6 @@ def i4g():
 def sk_case(i4g, M, N, K, grp, seed=0, a_dist="normal"):
     a, w = make_inputs(M, N, K, seed_a=311 + seed, seed_b=313 + seed, a_dist=a_dist)
     a16, w16 = u16(a), u16(w)
-    packed_np, scales_np = oracle.quantize(w16, K, N, grp)
     lin = i4g.QuantizedLinear.from_weight(w.cuda(), grp)
     need = i4g.gemm_workspace_size(M, N, K)
     ws = torch.zeros(max(need, 256), dtype=torch.uint8, device="cuda")
@@ -43,11 +42,8 @@ def sk_case(i4g, M, N, K, grp, seed=0, a_dist="normal"):
     torch.cuda.synchronize()
     assert i4g.device_status() == 0
     assert int(ws[:TICKET_BYTES].count_nonzero()) == 0, "arrival counters not reset"
-    deq = oracle.dequantize(packed_np, scales_np, K, N, grp)
-    rows = np.arange(M)
-    ref32 = oracle.gemm_rows(a16, deq, M, N, K, rows=rows, threads=8)
-    abs32 = oracle.abs_gemm_rows(a16, deq, M, N, K, rows=rows)
-    return gemm_report(u16(c), ref32, abs32, K), c, (a, lin, ws, need, ref32, abs32)
+    exp, _ = oracle_case(a16, w16, M, N, K, grp)
+    return gemm_report(u16(c), exp), c, (a, lin, ws, need, exp)
 
 
 @pytest.mark.parametrize("M,N,K,grp", [
@@ -63,13 +59,13 @@ def test_decode_streamk_parity(i4g, M, N, K, grp):
     assert i4g.gemm_workspace_size(M, N, K) >= need
     rep, _, _ = sk_case(i4g, M, N, K, grp)
     print("decode stream-k", M, N, K, grp, "grid", grid, rep)
-    assert rep["ok"], rep
+    assert_gemm_parity(rep)
 
 
 def test_decode_streamk_deterministic_and_close_to_cluster(i4g):
     M, N, K, grp = 4, 14336, 4096, 128
-    rep0, c0, (a, lin, ws, _, ref32, abs32) = sk_case(i4g, M, N, K, grp)
-    assert rep0["ok"], rep0
+    rep0, c0, (a, lin, ws, _, exp) = sk_case(i4g, M, N, K, grp)
+    assert_gemm_parity(rep0)
     ad = a.cuda()
     outs = []
     for _ in range(4):
@@ -80,16 +76,16 @@ def test_decode_streamk_deterministic_and_close_to_cluster(i4g):
     for o in outs:
         assert torch.equal(o.view(torch.int16), c0.view(torch.int16))
     # the cluster schedule (no workspace) sums the same products in another
-    # order; both meet the oracle tolerance, which bounds the FP32 order
-    # error (it exceeds an FP16 ulp only for outputs near zero)
+    # order; both meet the parity gate (the FP32 order changes an FP16
+    # output by more than an ulp only near zero)
     cl = torch.empty(M, N, dtype=torch.float16, device="cuda")
     i4g.launch_final(ad, lin.tiles, lin.scales, cl, M, N, K, grp)
     torch.cuda.synchronize()
-    rep1 = gemm_report(u16(cl), ref32, abs32, K)
+    rep1 = gemm_report(u16(cl), exp)
     ulp = oracle.ulp_distance(u16(cl), u16(c0))
     print("stream-k vs cluster: max ulp", int(ulp.max()), "identical",
           float((ulp == 0).mean()), rep1)
-    assert rep1["ok"], rep1
+    assert_gemm_parity(rep1)
     assert float((ulp <= 1).mean()) > 0.99
 
 

@@ -60,6 +60,24 @@ def _worker(rank, world, port, q, M, N, K, group):
         torch.cuda.synchronize()
         ok = ok and i4g.device_status() == 0
         outs.close()
+        # back-to-back calls with no host synchronisation while the last rank
+        # reads each result late (a sleep kernel before its copy): the reuse
+        # rule (two alternating buffers, or one buffer with an entry barrier)
+        # keeps a fast rank's next peer stores off a buffer still being read
+        for slots in (2, 1):
+            outs = PeerOutputs(M, N, a.device, slots=slots)
+            a_list = [(torch.rand(M, K, generator=g) * 2 - 1).half().cuda() for _ in range(4)]
+            copies = []
+            for a_it in a_list:
+                view = cp.forward_to_peers(a_it, outs)
+                if rank == world - 1:
+                    torch.cuda._sleep(4_000_000)  # ~2 ms: this rank reads late
+                copies.append(view.clone())
+            torch.cuda.synchronize()
+            for a_it, got in zip(a_list, copies):
+                ok = ok and bool(torch.equal(got.view(torch.int16), full(a_it).view(torch.int16)))
+            ok = ok and i4g.device_status() == 0
+            outs.close()
         flags = [None] * world
         dist.all_gather_object(flags, ok)
         if rank == 0:

@@ -12,7 +12,7 @@ import pytest
 import torch
 
 import oracle
-from parity import fp32_report, gemm_report, make_inputs, u16
+from parity import assert_gemm_parity, fp32_report, gemm_report, make_inputs, oracle_case, u16
 from plans import TICKET_BYTES, expected_plan, expected_workspace
 
 pytestmark = pytest.mark.gpu
@@ -43,7 +43,6 @@ def test_workspace_size(i4g, M, N, K):
 def split_case(i4g, M, N, K, grp, rows=None, fp32_out=False, seed=0):
     a, w = make_inputs(M, N, K, seed_a=99 + seed, seed_b=77 + seed)
     a16, w16 = u16(a), u16(w)
-    packed_np, scales_np = oracle.quantize(w16, K, N, grp)
     lin = i4g.QuantizedLinear.from_weight(w.cuda(), grp)
     ws, need = fresh_workspace(i4g, M, N, K)
     dt = torch.float32 if fp32_out else torch.float16
@@ -53,14 +52,11 @@ def split_case(i4g, M, N, K, grp, rows=None, fp32_out=False, seed=0):
     torch.cuda.synchronize()
     assert i4g.device_status() == 0
     assert int(ws[:TICKET_BYTES].count_nonzero()) == 0, "arrival counters not reset"
-    deq = oracle.dequantize(packed_np, scales_np, K, N, grp)
-    rows = np.arange(M) if rows is None else np.asarray(rows)
-    ref32 = oracle.gemm_rows(a16, deq, M, N, K, rows=rows, threads=8)
-    abs32 = oracle.abs_gemm_rows(a16, deq, M, N, K, rows=rows)
+    exp, _ = oracle_case(a16, w16, M, N, K, grp, rows)
     if fp32_out:
-        rep = fp32_report(c.cpu().numpy()[rows], ref32, abs32, K)
+        rep = fp32_report(c.cpu().numpy()[exp.rows], exp)
     else:
-        rep = gemm_report(u16(c)[rows], ref32, abs32, K)
+        rep = gemm_report(u16(c)[exp.rows], exp)
     return rep, c, (a.cuda(), lin, ws)
 
 
@@ -78,7 +74,7 @@ def test_split_parity(i4g, M, N, K, grp, kind):
     assert expected_plan(M, N, K)[0] == kind, "shape chosen to exercise this schedule"
     rep, _, _ = split_case(i4g, M, N, K, grp, rows=sample_rows(M, M + N))
     print(kind, M, N, K, grp, rep)
-    assert rep["ok"], rep
+    assert_gemm_parity(rep)
 
 
 @pytest.mark.parametrize("grp", [32, 128])
@@ -91,7 +87,7 @@ def test_split_4096_sampled_rows(i4g, grp):
                            np.arange(4088, 4096)])
     rep, _, _ = split_case(i4g, M, N, K, grp, rows=rows)
     print("split 4096^3 g", grp, rep)
-    assert rep["ok"], rep
+    assert_gemm_parity(rep)
 
 
 @pytest.mark.parametrize("M,N,K,grp", [(512, 1024, 4096, 64), (2048, 640, 8192, 128)])
@@ -157,7 +153,7 @@ def test_stream_k_tail_parity(i4g, M, N, K, grp):
     assert expected_plan(M, N, K)[0] == "stream-k"
     rep, c, (a, lin, ws) = split_case(i4g, M, N, K, grp, rows=sample_rows(M, K))
     print("stream-k", M, N, K, grp, rep)
-    assert rep["ok"], rep
+    assert_gemm_parity(rep)
     c2 = torch.empty_like(c)
     i4g.launch_final_ws(a, lin.tiles, lin.scales, c2, M, N, K, grp, ws)
     torch.cuda.synchronize()
@@ -178,10 +174,5 @@ def test_smaller_workspace_falls_back_to_equal_splits(i4g):
     torch.cuda.synchronize()
     assert i4g.device_status() == 0
     assert int(ws[:TICKET_BYTES].count_nonzero()) == 0
-    a16 = u16(a)
-    packed, scales = oracle.quantize(u16(w), K, N, 128)
-    deq = oracle.dequantize(packed, scales, K, N, 128)
-    rows = np.array([0, 1, 2047, 3000, 4095])
-    rep = gemm_report(u16(c)[rows], oracle.gemm_rows(a16, deq, M, N, K, rows=rows, threads=8),
-                      oracle.abs_gemm_rows(a16, deq, M, N, K, rows=rows), K)
-    assert rep["ok"], rep
+    exp, _ = oracle_case(u16(a), u16(w), M, N, K, 128, np.array([0, 1, 2047, 3000, 4095]))
+    assert_gemm_parity(gemm_report(u16(c)[exp.rows], exp))

@@ -126,3 +126,83 @@ int main() {
     out = subprocess.run([str(exe)], capture_output=True, text=True)
     assert out.returncode == 0, out
     assert "null pointer" in out.stdout
+
+
+def test_kernel_config_needs_no_gpu():
+    import sm_120__gemm_b200 as m
+    c = m.kernel_config(m.VARIANT_TC, 256, 128)
+    assert (c["rows"], c["cols"], c["bk"], c["mma_m"], c["mma_n"]) == (256, 128, 64, 128, 256)
+    assert c["threads"] == 864 and 0 < c["dynamic_smem_bytes"] <= 232448
+    d = m.kernel_config(m.VARIANT_DECODE, 16, 64)
+    assert d["rows"] == 16 and d["cols"] == 128 and d["stages"] >= 2
+    with pytest.raises(m.I4GError):
+        m.kernel_config(m.VARIANT_TC, 64, 128)
+    with pytest.raises(m.I4GError):
+        m.kernel_config(m.VARIANT_DECODE, 8, 96)
+
+
+def test_cpp_registry_matches_the_reference_interface(tmp_path):
+    """kernel_registry() / KernelMetadata / query_resources() of
+    include/int4gemm.hpp, used the way the reference's harness uses them
+    (src/main.cu:247-249, 349-377); without a GPU the resource query throws."""
+    import shutil
+    import subprocess
+    if shutil.which("g++") is None:
+        pytest.skip("no host C++ compiler")
+    src = tmp_path / "r.cpp"
+    src.write_text(r'''
+#include "int4gemm.hpp"
+#include <cstdio>
+int main() {
+  using namespace int4gemm;
+  auto reg = kernel_registry();
+  if (reg.size() != 1) return 2;
+  const KernelMetadata& md = reg[0].first;
+  KernelLaunch fn = reg[0].second;
+  std::printf("%s BM=%d BN=%d BK=%d mma=%dx%d stages=%d threads=%d smem=%d\n", md.version,
+              md.BM, md.BN, md.BK, md.warp_m, md.warp_n, md.stages, md.threads, md.smem_bytes);
+  if (fn != &launch_final) return 3;
+  try { KernelResources r = query_resources(md.version, 128); (void)r; }
+  catch (const std::runtime_error& e) { std::printf("resources threw\n"); }
+  try { query_resources("v17b", 128); return 4; } catch (const std::runtime_error&) {}
+  return 0;
+}
+''')
+    exe = tmp_path / "r"
+    pkg = os.path.join(ROOT, "sm_120__gemm_b200")
+    subprocess.run(["g++", "-std=c++17", "-I", os.path.join(ROOT, "include"),
+                    "-I", "/usr/local/cuda/include", str(src), "-o", str(exe),
+                    "-L", pkg, "-li4g", f"-Wl,-rpath,{pkg}"], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert out.returncode == 0, out
+    assert out.stdout.startswith("final BM=256 BN=128 BK=64 mma=128x256"), out.stdout
+
+
+def _reference_checkout():
+    import json
+    path = os.environ.get("I4G_REFERENCE")
+    if not path:
+        with open(os.path.join(ROOT, "BASELINE.json")) as f:
+            path = json.load(f).get("reference_path")
+    return path if path and os.path.isfile(os.path.join(path, "src", "main.cu")) else None
+
+
+def test_reference_harness_builds_against_the_library(tmp_path):
+    """The reference's own harness (src/main.cu, with the one documented
+    layout change of oracle/harness_patch.py) and its CPU checker compile and
+    link against include/reference_compat + include/int4gemm.hpp +
+    libi4g.so. Needs the reference checkout (skipped where it is absent)."""
+    import subprocess
+    ref = _reference_checkout()
+    if ref is None:
+        pytest.skip("reference checkout not present")
+    out = tmp_path / "int4_gemm"
+    r = subprocess.run(["make", "-C", os.path.join(ROOT, "oracle"), "harness", f"REF={ref}",
+                        f"HARNESS_OUT={out}"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    assert out.exists()
+    patched = open(f"{out}_main.cu").read()
+    original = open(os.path.join(ref, "src", "main.cu")).read()
+    # the patch only adds lines or swaps a repack call for the tile repack
+    assert patched.count("use_tile_layout(x);") == 4
+    assert len(patched.splitlines()) - len(original.splitlines()) == 12

@@ -108,15 +108,23 @@ def test_compare_half_matches_reference_formula(oracle_mod):
 
 
 @pytest.mark.parametrize("name", golden_names("gemm_"))
-def test_fp64_attribution_of_the_reference_path(oracle_mod, name):
-    """The FP64 attribution used by the GPU parity reports: the reference's
-    own FP32 path, judged against the FP64 oracle, is the same distance from
-    it as itself (sanity) and at most a few ulps from it on these cases."""
-    from parity import fp64_attribution
+def test_parity_gate_on_the_reference_path(oracle_mod, name):
+    """The GEMM parity gate, applied to the reference's own output (the
+    fixture's c16, made by the reference's cpu_gemm_fp32): it passes with
+    every output at 0 ulps, and the exact-sum anchor puts the reference's
+    path within a few ulps of the exact answer on these cases. A planted
+    3-ulp error in the largest output fails the gate."""
+    from parity import gemm_report, reference_rows
     g = load_golden(name)
     M, N, K, grp = g["M"], g["N"], g["K"], g["group"]
     deq = oracle_mod.dequantize(g["packed"], g["scales"], K, N, grp)
-    rep = fp64_attribution(g["a"], deq, g["c16"], g["c32"])
-    assert rep["fp64_max_ulp_ours"] == rep["fp64_max_ulp_ref"]
-    assert rep["fp64_outputs_closer_ours"] == rep["fp64_outputs_closer_ref"] == 0
-    assert rep["fp64_max_ulp_ref"] <= 8, rep
+    exp = reference_rows(g["a"], deq, M, N, K, np.arange(M), threads=2)
+    np.testing.assert_array_equal(exp.ref32.view(np.uint32), g["c32"].view(np.uint32))
+    rep = gemm_report(g["c16"], exp)
+    assert rep["ok"] and rep["max_ulp"] == 0, rep
+    assert rep["max_ulp_vs_exact_ref"] <= 8, rep
+    planted = g["c16"].copy()
+    idx = np.unravel_index(np.argmax(np.abs(oracle_mod.h2f(planted))), planted.shape)
+    planted[idx] = planted[idx] + 3  # 3 ulps away (same sign, far from zero)
+    bad = gemm_report(planted, exp)
+    assert not bad["ok"] and bad["bad"] == 1, bad
