@@ -7,7 +7,14 @@ A step is the headline workload of configs[1]: three fused GEMMs at
 M=N=K=4096, one per group size (32, 64, 128), each on its own quantised
 weight, FP16 C. Under torchrun every rank owns its own 4096-column slice of
 a column-parallel weight (N_total = 4096 * world), so per-GPU work is fixed
-("weak" scaling) and no collective is on the data path.
+("weak" scaling), and every GEMM delivers the full [4096, N_total] C to every
+rank: by default its epilogue stores the rank's columns into every rank's C
+over NVLink and a flag barrier ends the call (--gather nccl: plain GEMM, then
+NCCL all-gather + permute). After the timing the gathered C is checked bit
+for bit against an NCCL gather of per-rank GEMMs. Extra blocks time configs[3]
+(prefill, strong scaling over the job's GPUs) and configs[4] (the M sweep with
+the gather), and at N = 1 the end-to-end path, the decode shapes, the
+reference's "separate" dequant + cuBLAS row and the CPU baseline.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -135,6 +142,7 @@ def run_ours(args, rank, world, local_rank):
     import torch.distributed as dist
 
     import sm_120__gemm_b200 as i4g
+    from sm_120__gemm_b200.sharded import PeerOutputs, gather_columns
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -142,7 +150,9 @@ def run_ours(args, rank, world, local_rank):
     M, K = M_HEAD, K_HEAD
     n_local = N_HEAD
     n_total = n_local * world
+    n0 = rank * n_local
     peaks = load_peaks()
+    gather = args.gather if world > 1 else "none"
 
     # Seeded synthetic inputs: A fp16 U[-1,1]; W fp32 N(0, 0.02) -> fp16 ->
     # quantised on the GPU (codes bit-identical to quantize_cpu). Each rank
@@ -154,14 +164,32 @@ def run_ours(args, rank, world, local_rank):
 
     # Rotating inputs keep each GEMM's operands out of L2 (126 MB) when the
     # GEMM runs: 4 activation buffers (32 MiB each) and 2 weight sets per group.
+    # The activations are the same on every rank (replicated A), as in a
+    # column-parallel layer.
     n_act, n_wset = 4, 2
-    gen_a = torch.Generator(device=dev).manual_seed(1234 + rank)
+    gen_a = torch.Generator(device=dev).manual_seed(1234)
     acts = [(torch.rand(M, K, generator=gen_a, device=dev) * 2 - 1).half() for _ in range(n_act)]
     lins = {g: [weights(g, r) for r in range(n_wset)] for g in GROUPS}
     outs = [torch.empty(M, n_local, dtype=torch.float16, device=dev) for _ in range(3)]
     # Split-K workspace for the last partial wave (None: whole tiles only).
     ws = i4g.workspace_for(M, n_local, K, dev, stream) if args.schedule == "split" else None
+    # At N > 1 every GEMM also delivers the full [M, N_total] C to every rank:
+    # "fused" stores each rank's columns straight into every rank's C from the
+    # GEMM epilogue (i4g_gemm_to_peers) and ends with the flag barrier;
+    # "nccl" runs the plain GEMM, then an NCCL all-gather and the permute.
+    peer = PeerOutputs(M, n_total, dev) if gather == "fused" else None
+    full = torch.empty(M, n_total, dtype=torch.float16, device=dev) if gather == "nccl" else None
+    gbuf = (torch.empty(world * M * n_local, dtype=torch.float16, device=dev)
+            if gather == "nccl" else None)
     torch.cuda.synchronize()
+
+    def gemm(lin, a, g, j):
+        if peer is not None:
+            dsts = peer.begin_call(stream)
+            i4g.launch_final_to_peers(a, lin.tiles, lin.scales, dsts, n_total, n0, M, n_local, K,
+                                      g, ws, stream)
+        else:
+            i4g.launch_final_ws(a, lin.tiles, lin.scales, outs[j], M, n_local, K, g, ws, stream)
 
     def step(i, events=None):
         for j, g in enumerate(GROUPS):
@@ -169,9 +197,13 @@ def run_ours(args, rank, world, local_rank):
             a = acts[(3 * i + j) % n_act]
             if events is not None:
                 events[j][0].record(stream)
-            i4g.launch_final_ws(a, lin.tiles, lin.scales, outs[j], M, n_local, K, g, ws, stream)
+            gemm(lin, a, g, j)
             if events is not None:
                 events[j][1].record(stream)
+            if peer is not None:
+                peer.barrier(stream)
+            elif gather == "nccl":
+                gather_columns(outs[j], out=full, gathered=gbuf)
 
     for i in range(args.warmup):
         step(i)
@@ -204,11 +236,29 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
 
+    # The gathered C of the last GEMM, checked bit for bit on every rank
+    # against an NCCL all-gather of per-rank plain GEMMs (outside the timing).
+    gather_check = None
+    if gather != "none":
+        last = args.warmup + args.steps - 1
+        g = GROUPS[-1]
+        lin = lins[g][(last + len(GROUPS) - 1) % n_wset]
+        a = acts[(3 * last + len(GROUPS) - 1) % n_act]
+        got = (peer.view(M) if peer is not None else full).clone()
+        ref = gather_columns(lin(a))
+        same = torch.tensor([float(torch.equal(got.view(torch.int16), ref.view(torch.int16)))],
+                            device=dev)
+        dist.all_reduce(same, op=dist.ReduceOp.MIN)
+        gather_check = bool(same.item() == 1.0)
+
     step_flops_rank = sum(flops(M, n_local, K) for _ in GROUPS)
     value = step_flops_rank * world * args.steps / (ms_max * 1e-3) / 1e12
     kernel_ms = {g: statistics.mean(v) for g, v in per_group_ms.items()}
     kernel_total_ms = sum(kernel_ms.values())
     achieved = step_flops_rank / (kernel_total_ms * 1e-3) / 1e12
+    gather_desc = {"none": "none (one GPU)" if world == 1 else "none",
+                   "fused": "fused: GEMM epilogue stores into every rank's C + flag barrier",
+                   "nccl": "NCCL all_gather_into_tensor + permute after each GEMM"}[gather]
     result = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
@@ -216,32 +266,183 @@ def run_ours(args, rank, world, local_rank):
         "data": "synthetic (seeded): A fp16 U[-1,1]; W fp32 N(0,0.02) -> fp16 -> INT4",
         "config": {"workload": WORKLOAD, "M": M, "N_per_gpu": n_local, "N_total": n_total,
                    "K": K, "groups": list(GROUPS), "parallelism": f"column-parallel x{world}",
+                   "gather": gather_desc,
                    "l2": "rotating inputs: 4 x 32 MiB activations, 2 weight sets per group",
                    "schedule": args.schedule + (f" (workspace {ws.numel()} B)" if ws is not None
                                                 else "")},
         "per_group": {str(g): {"kernel_ms": round(kernel_ms[g], 4),
                                "tflops": round(flops(M, n_local, K) / kernel_ms[g] / 1e9, 1)}
                       for g in GROUPS},
-        "gpu_launches": args.steps * len(GROUPS),
+        "gpu_launches": args.steps * len(GROUPS) * (2 if peer is not None else 1),
     }
+    if gather_check is not None:
+        result["gather_check"] = {"bitwise_equal_to_nccl_gather_on_every_rank": gather_check}
     traffic = load_profile_traffic().get("tc_4096_g128_bytes_per_launch")
     result["roofline"] = {
         "bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"],
         "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
         "traffic": traffic,
         "peak_source": f"{peaks['source']} (cuBLAS bf16 burst; fp16 dense runs at the bf16 rate)",
-        "kernel": "gemm_tc_kernel (tcgen05, TMEM)",
+        "kernel": "gemm_tc_kernel (tcgen05, TMEM)" + (", with peer stores" if peer else ""),
         "algorithmic_bytes_per_launch": algorithmic_bytes(M, n_local, K, 128),
     }
     result["clocks"] = clocks.summary()
+    if peer is not None:
+        peer.close()
+    del outs, full, gbuf, peer
+    torch.cuda.empty_cache()
 
+    if not args.no_extras:
+        result["prefill_strong"] = run_prefill(args, i4g, rank, world, dev)
+        result["m_sweep"] = run_m_sweep(args, i4g, rank, world, dev)
     if rank == 0 and world == 1 and not args.no_extras:
         result["e2e"] = run_e2e(args, i4g, lins, dev)
         result["decode"] = run_decode(args, i4g, dev, peaks)
+        result["separate_baseline"] = run_separate(args, i4g, lins, dev)
         result["cpu_baseline"] = cpu_baseline(args, sample_rows=args.cpu_rows)
     elif rank == 0:
         result["e2e"] = run_e2e(args, i4g, lins, dev)
     return result
+
+
+def _time_max(fn, iters, dev, world):
+    """Device time per call of fn (CUDA events on the current stream, after 3
+    warm-ups), max over ranks."""
+    import torch
+    import torch.distributed as dist
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    b, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    b.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    e.synchronize()
+    t = torch.tensor([b.elapsed_time(e) * 1e3 / iters], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _column_parallel(i4g, rank, world, dev, K, N, g, seed):
+    import torch
+    from sm_120__gemm_b200.sharded import ColumnParallelLinear
+    n_local = N // world
+    gen = torch.Generator(device=dev).manual_seed(seed + rank)
+    w = (torch.randn(K, n_local, generator=gen, device=dev) * 0.02).half()
+    lin = i4g.QuantizedLinear.from_weight(w, g)
+    del w
+    return ColumnParallelLinear(lin, world, rank), n_local
+
+
+def run_prefill(args, i4g, rank, world, dev):
+    """M=8192, K=8192, N=28672, g128, column-parallel over the job's
+    G = world GPUs (N/G columns each; strong scaling across G). Per call: the
+    GEMM alone and the GEMM with the full C delivered to every rank (fused
+    gather) when G > 1; whole-job TFLOP/s from the max-over-ranks time."""
+    import torch
+    from sm_120__gemm_b200.sharded import PeerOutputs
+    M, K, N, g = 8192, 8192, 28672, 128
+    cp, n_local = _column_parallel(i4g, rank, world, dev, K, N, g, 777)
+    a = (torch.rand(M, K, generator=torch.Generator(device=dev).manual_seed(31), device=dev)
+         * 2 - 1).half()
+    c = torch.empty(M, n_local, dtype=torch.float16, device=dev)
+    gemm_us = _time_max(lambda: cp.forward_local(a, out=c), args.extra_iters, dev, world)
+    out = {"workload": "configs[3]: M=8192 K=8192 N=28672 g128, column-parallel",
+           "G": world, "N_per_gpu": n_local, "gemm_us": round(gemm_us, 1),
+           "gemm_tflops": round(2.0 * M * N * K / (gemm_us * 1e-6) / 1e12, 1)}
+    if world > 1:
+        peer = PeerOutputs(M, N, dev)
+        e2e_us = _time_max(lambda: cp.forward_to_peers(a, peer), args.extra_iters, dev, world)
+        peer.close()
+        out.update({"gemm_plus_fused_gather_us": round(e2e_us, 1),
+                    "e2e_tflops": round(2.0 * M * N * K / (e2e_us * 1e-6) / 1e12, 1)})
+        del peer
+    del cp, a, c
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_m_sweep(args, i4g, rank, world, dev):
+    """K=8192, N=57344 (fused gate+up), g64, each rank N/G columns
+    (the config names G = 8); per M, the kernel the dispatcher picks, the GEMM
+    alone and, when G > 1, the GEMM with the full C on every rank by the fused
+    gather and by NCCL all-gather + permute (max-over-ranks device times)."""
+    import torch
+    from sm_120__gemm_b200.sharded import PeerOutputs, gather_columns
+    K, N, g = 8192, 57344, 64
+    cp, n_local = _column_parallel(i4g, rank, world, dev, K, N, g, 9000)
+    gen = torch.Generator(device=dev).manual_seed(4321)
+    res = {"workload": "configs[4]: K=8192 N=57344 g64, column-parallel", "G": world,
+           "N_per_gpu": n_local}
+    for M in (1, 16, 128, 1024, 4096, 16384):
+        a = (torch.rand(M, K, generator=gen, device=dev) * 2 - 1).half()
+        c = torch.empty(M, n_local, dtype=torch.float16, device=dev)
+        p = i4g.plan(M, n_local, K, g, torch.cuda.get_device_properties(dev).multi_processor_count,
+                     i4g.gemm_workspace_size(M, n_local, K))
+        row = {"kernel": p["kernel"], "schedule": p["schedule"]}
+        row["gemm_us"] = round(_time_max(lambda: cp.forward_local(a, out=c), args.extra_iters,
+                                         dev, world), 2)
+        if world > 1:
+            peer = PeerOutputs(M, N, dev)
+            row["fused_gather_us"] = round(_time_max(lambda: cp.forward_to_peers(a, peer),
+                                                     args.extra_iters, dev, world), 2)
+            full = torch.empty(M, N, dtype=torch.float16, device=dev)
+            gbuf = torch.empty(world * M * n_local, dtype=torch.float16, device=dev)
+
+            def nccl():
+                cp.forward_local(a, out=c)
+                gather_columns(c, out=full, gathered=gbuf)
+
+            row["nccl_gather_us"] = round(_time_max(nccl, args.extra_iters, dev, world), 2)
+            # each rank receives (G-1)/G of C over NVLink
+            row["gather_bytes_in_per_rank"] = (world - 1) * M * n_local * 2
+            peer.close()
+            del peer, full, gbuf
+        res[f"M{M}"] = row
+        del a, c
+        torch.cuda.empty_cache()
+    del cp
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_separate(args, i4g, lins, dev):
+    """The reference's "separate" comparison row (src/main.cu:319): the
+    dequantize kernel materialises B in FP16, then cuBLAS (torch.matmul) runs
+    the FP16 GEMM, at the headline shape, g128; beside the fused kernel."""
+    import torch
+    M, N, K, g = M_HEAD, N_HEAD, K_HEAD, 128
+    gen = torch.Generator(device=dev).manual_seed(55)
+    w = (torch.randn(K, N, generator=gen, device=dev) * 0.02).half()
+    packed = torch.empty(K * N // 2, dtype=torch.uint8, device=dev)
+    scales = torch.empty(K // g, N, dtype=torch.float16, device=dev)
+    i4g.launch_quantize(w, packed, scales, K, N, g)
+    lin = i4g.QuantizedLinear.from_packed(packed, scales, K, N, g)
+    b16 = torch.empty(K, N, dtype=torch.float16, device=dev)
+    a = (torch.rand(M, K, generator=gen, device=dev) * 2 - 1).half()
+    c = torch.empty(M, N, dtype=torch.float16, device=dev)
+    ws = i4g.workspace_for(M, N, K, dev)
+
+    def separate():
+        i4g.launch_dequantize(packed, scales, b16, K, N, g)
+        torch.matmul(a, b16, out=c)
+
+    def fused():
+        i4g.launch_final_ws(a, lin.tiles, lin.scales, c, M, N, K, g, ws)
+
+    out = {}
+    for name, fn in (("dequant_plus_cublas_us", separate),
+                     ("cublas_fp16_only_us", lambda: torch.matmul(a, b16, out=c)),
+                     ("fused_us", fused)):
+        out[name] = round(_time_max(fn, 50, dev, 1), 1)
+    out["fused_speedup_vs_separate"] = round(out["dequant_plus_cublas_us"] / out["fused_us"], 3)
+    out["note"] = ("M=N=K=4096 g128, warm L2 (same operands each call); the reference's "
+                   "'separate' and 'cublas_fp16' rows")
+    return out
 
 
 def run_e2e(args, i4g, lins, dev):
@@ -459,8 +660,12 @@ def main():
     ap.add_argument("--schedule", choices=["split", "whole"], default="split",
                     help="split: split-K the last partial wave through a workspace; "
                          "whole: whole output tiles only (i4g_gemm)")
+    ap.add_argument("--gather", choices=["fused", "nccl", "none"], default="fused",
+                    help="at N > 1, how each GEMM's full C reaches every rank")
+    ap.add_argument("--extra-iters", type=int, default=10,
+                    help="calls timed per shape in the prefill / M-sweep blocks")
     ap.add_argument("--no-extras", action="store_true",
-                    help="skip the e2e / decode / cpu-baseline legs")
+                    help="skip the prefill, M-sweep, e2e, decode and cpu-baseline legs")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -246,6 +246,16 @@ int gemm_common(const void* A, const uint8_t* tiles, const void* scales, const i
   if (out.col0 < 0 || out.ldc < out.col0 + N)
     return fail(I4G_ERR_SHAPE, "columns [%d, %d) do not fit rows of %d", out.col0, out.col0 + N,
                 out.ldc);
+  if (out.count > 1) {
+    // peer copies move in 16-byte pieces: every copy, its row stride and the
+    // column offset must keep 16-byte alignment
+    if (out.ldc % 8 != 0 || out.col0 % 8 != 0)
+      return fail(I4G_ERR_ALIGNMENT, "ldc (%d) and col0 (%d) must be multiples of 8 with copies",
+                  out.ldc, out.col0);
+    for (int d = 0; d < out.count; ++d)
+      if (!aligned(out.dst[d], 16))
+        return fail(I4G_ERR_ALIGNMENT, "C copies must be 16-byte aligned");
+  }
   int st = check_shape(M, N, K);
   if (st != I4G_OK) return st;
   st = check_group(K, group, true);

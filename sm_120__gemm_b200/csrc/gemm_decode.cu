@@ -360,6 +360,7 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM)
   const uint32_t bars = ring + L::BARS;  // full[STAGES], empty[STAGES]
   float* partial = reinterpret_cast<float*>(smem + L::PARTIAL);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::ABORT);
+  volatile int* never = abort_flag + 2;  // a flag nobody sets (draining waits)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -378,6 +379,7 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM)
       mbar_init(bars + 8 * (STAGES + s), CWARPS);
     }
     *abort_flag = 0;
+    *never = 0;
     fence_mbarrier_init();
     fence_proxy_async_smem();
   }
@@ -398,9 +400,8 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM)
                                        kblocks, groups, ring + s * L::SLOT, bars + 8 * s);
       }
       if (issued < nstages) {  // gave up: let the copies already issued land first
-        volatile int never = 0;
         for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; ++i)
-          mbar_wait(bars + 8 * (i % STAGES), (i / STAGES) & 1u, &never, nullptr, 100000000ull);
+          mbar_wait(bars + 8 * (i % STAGES), (i / STAGES) & 1u, never, nullptr, 100000000ull);
       }
     }
   } else {
@@ -503,6 +504,7 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM)
   const uint32_t ring = smem_u32(smem);
   const uint32_t bars = ring + L::BARS;  // full[STAGES], empty[STAGES]
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::ABORT);
+  volatile int* never = abort_flag + 2;  // a flag nobody sets (draining waits)
   volatile int* last_flag = abort_flag + 1;  // "this CTA reduces the tile", per segment
 
   const int warp = threadIdx.x >> 5;
@@ -521,6 +523,7 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM)
       mbar_init(bars + 8 * (STAGES + s), CWARPS);
     }
     *abort_flag = 0;
+    *never = 0;
     fence_mbarrier_init();
     fence_proxy_async_smem();
   }
@@ -551,9 +554,8 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM)
         u = static_cast<long>(nt) * kblocks + kb_end;
       }
       if (!ok) {  // gave up: let the copies already issued land first
-        volatile int never = 0;
         for (int j = (issued > STAGES ? issued - STAGES : 0); j < issued; ++j)
-          mbar_wait(bars + 8 * (j % STAGES), (j / STAGES) & 1u, &never, nullptr, 100000000ull);
+          mbar_wait(bars + 8 * (j % STAGES), (j / STAGES) & 1u, never, nullptr, 100000000ull);
       }
     }
     return;

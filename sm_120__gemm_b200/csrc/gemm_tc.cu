@@ -33,6 +33,15 @@
 // The weight ring does not wait for the tensor core, so the dequant runs
 // ahead of the MMA by up to T_STAGES blocks.
 //
+// Accumulation accuracy: the tensor core's FP32 accumulator drifts further
+// from the exact sum than a sequential round-to-nearest FP32 sum as the chain
+// of MMAs onto it grows. So every `promo` 64-k blocks the epilogue warps fold
+// the accumulator into a running sum (promotion): S = H + D rounded once in
+// FP32, a coarse H (FP8) kept in registers, and the exact remainder S - H written
+// back into the accumulator, onto which the next MMAs accumulate. The tile's
+// result is H + D. The chain the tensor core accumulates stays short whatever K
+// is.
+//
 // Schedule: work items are whole tiles, round robin over the grid; then,
 // when the caller provides a workspace, the tiles of the last, partial wave
 // ("tail") are shared out along K so that the last wave keeps every SM busy:
@@ -46,7 +55,11 @@
 #include "ptx.cuh"
 #include "gemm_tc.h"
 
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
+
+#include <climits>
+#include <cstdlib>
 
 namespace i4g {
 namespace tc {
@@ -108,7 +121,7 @@ struct Item {
 };
 
 // Work of CTA `b` of a grid of `g`: its `j`-th item, false past its last.
-static __device__ __noinline__ bool next_item(const Sched& s, int b, int g, int j, int kblocks,
+__device__ __forceinline__ bool next_item(const Sched& s, int b, int g, int j, int kblocks,
                                           int num_m, int num_n, Item& r) {
   int tile;
   if (s.chunks == 0) {
@@ -247,6 +260,131 @@ __device__ __forceinline__ void tmem_ld_wait16(uint32_t (&r)[16]) {
                : "memory");
 }
 
+// Running sum of promotion. Its high part H is kept coarse, in FP8 (e5m2,
+// saturating), four values per 32-bit register: any H leaves the remainder
+// S - H exact in FP32 (S has 24 significant bits, H 3 at the same or the next
+// exponent), and a coarse H costs the epilogue warps few registers.
+__device__ __forceinline__ float2 e5m2x2_to_float2(uint32_t pair) {
+  const __half2_raw r = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(pair),
+                                                   __NV_E5M2);
+  __half2 h;
+  memcpy(&h, &r, sizeof(h));
+  return __half22float2(h);
+}
+
+__device__ __forceinline__ uint32_t float2_to_e5m2x2(float lo, float hi) {
+  return static_cast<uint32_t>(
+      __nv_cvt_float2_to_fp8x2(make_float2(lo, hi), __NV_SATFINITE, __NV_E5M2));
+}
+
+// H of accumulator columns 4q .. 4q+3 of one lane, from word q of hb.
+__device__ __forceinline__ void high_parts(uint32_t w, float (&h)[4]) {
+  const float2 a = e5m2x2_to_float2(w & 0xFFFFu), b = e5m2x2_to_float2(w >> 16);
+  h[0] = a.x;
+  h[1] = a.y;
+  h[2] = b.x;
+  h[3] = b.y;
+}
+
+// Promotes 8 accumulator columns at taddr (hb words 0, 1): S = H + D (one
+// FP32 rounding per value), H <- e5m2(S), D <- S - H (exact), stored back.
+__device__ __forceinline__ void promote_chunk(uint32_t taddr, uint32_t* hb) {
+  uint32_t v[8];
+  tmem_ld_32x32b_x8(taddr, v);
+  tmem_ld_wait8(v);
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    float h[4], sum[4];
+    high_parts(hb[q], h);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sum[i] = h[i] + __uint_as_float(v[4 * q + i]);
+    hb[q] = float2_to_e5m2x2(sum[0], sum[1]) | (float2_to_e5m2x2(sum[2], sum[3]) << 16);
+    high_parts(hb[q], h);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[4 * q + i] = __float_as_uint(sum[i] - h[i]);
+  }
+  tmem_st_32x32b_x8(taddr, v);
+}
+
+// Final read of 16 accumulator columns (hb words 0..3): v = H + D in FP32.
+__device__ __forceinline__ void load_sum16(uint32_t taddr, const uint32_t* hb, uint32_t (&v)[16]) {
+  tmem_ld_32x32b_x16(taddr, v);
+  tmem_ld_wait16(v);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    float h[4];
+    high_parts(hb[q], h);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[4 * q + i] = __float_as_uint(h[i] + __uint_as_float(v[4 * q + i]));
+  }
+}
+
+// Moves words 4.. of a running-sum array down by four, so that a rolled loop
+// over 16-column chunks always reads words 0..3 (static register indices).
+template <int NW>
+__device__ __forceinline__ void shift_down4(uint32_t (&hb)[NW]) {
+#pragma unroll
+  for (int q = 0; q + 4 < NW; ++q) hb[q] = hb[q + 4];
+}
+
+// Whole-tile epilogue with several copies of C (this GPU's and peers'), for
+// one thread's slice (TMEM lane `row`, COLS accumulator columns from col0):
+// the slice is read, converted and the accumulator released as in the plain
+// path, then stored into this GPU's copy (dst[0]). Once every epilogue thread
+// has stored its slice (GPU-scope fence, then the epilogue barrier) the
+// finished tile is read back from L2 and copied to the peers' copies in
+// 16-byte pieces, so the NVLink traffic moves in full 16-byte stores and the
+// next tile's MMAs never wait on it. Every epilogue thread takes the barrier
+// whatever `ok` is (a failed wait skips the work, never the barrier).
+template <int TILE_M>
+__device__ __forceinline__ void copies_epilogue(bool ok, const Outputs& out, int M, int mt, int nt,
+                                             int half, int row, int m0, uint32_t col0,
+                                             const uint32_t* hb, uint32_t empty_bar, int epi_warp,
+                                             int lane) {
+  constexpr int COLS = TILE_M / 4;
+  constexpr int EPI_THREADS = NUM_EPI_WARPS * 32;
+  const size_t ldc = static_cast<size_t>(out.ldc);
+  const size_t tile_off = static_cast<size_t>(mt * TILE_M) * ldc + out.col0 + nt * TILE_N;
+  __half* const tile0 = static_cast<__half*>(out.dst[0]) + tile_off;
+  if (ok) {
+    tc_fence_after();
+    uint32_t h[COLS / 2];  // packed halves: h[j] = columns 2j, 2j+1
+#pragma unroll
+    for (int c = 0; c < COLS / 16; ++c) {
+      uint32_t v[16];
+      load_sum16(col0 + c * 16, &hb[c * 4], v);
+      pack_half2(v, &h[c * 8], 8);
+    }
+    tc_fence_before();
+    mbar_arrive(empty_bar);
+    __half* cp = tile0 + static_cast<size_t>(half * COLS) * ldc + row;
+    const int valid = min(COLS, M - m0);
+#pragma unroll
+    for (int j = 0; j < COLS / 2; ++j) {
+      const __half2 p2 = *reinterpret_cast<const __half2*>(&h[j]);
+      if (2 * j < valid) *cp = __low2half(p2);
+      cp += ldc;
+      if (2 * j + 1 < valid) *cp = __high2half(p2);
+      cp += ldc;
+    }
+  }
+  if (out.count == 1) return;
+  __threadfence();
+  if (!epi_bar_and(EPI_THREADS, ok)) return;
+  const int rows = min(TILE_M, M - mt * TILE_M);
+  // 16 pieces of 16 bytes per 128-column row; consecutive threads take
+  // consecutive pieces of a row
+#pragma unroll 1
+  for (int piece = epi_warp * 32 + lane; piece < rows * 16; piece += EPI_THREADS) {
+    const size_t off = static_cast<size_t>(piece >> 4) * ldc + (piece & 15) * 8;
+    const uint4 v = __ldcg(reinterpret_cast<const uint4*>(tile0 + off));
+#pragma unroll 1
+    for (int d = 1; d < out.count; ++d)
+      *reinterpret_cast<uint4*>(static_cast<__half*>(out.dst[d]) + tile_off + off) = v;
+  }
+  __threadfence_system();  // peer copies are read by other GPUs
+}
+
 // OUT selects the C epilogue at compile time, so the plain kernels carry no
 // code for the general one: half C or float C as one row-major [M][N] matrix
 // (out.dst[0]; ldc == N, col0 == 0), or half C written to columns
@@ -292,6 +430,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC_OFF + 4);
   volatile uint32_t* ticket_slot = reinterpret_cast<volatile uint32_t*>(smem + L::MISC_OFF + 8);
+  // a flag nobody sets: the "abort" of the bounded waits that must not be cut
+  // short by another warp's abort (draining copies, the final MMA drain)
+  volatile int* never = reinterpret_cast<volatile int*>(smem + L::MISC_OFF + 12);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -319,6 +460,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
+    *never = 0;
     fence_mbarrier_init();
     fence_proxy_async_smem();
   }
@@ -336,8 +478,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------- activation producer
     if (lane == 0) {
       uint32_t it = 0;
-      int last_issue[A_STAGES];
-      for (int s = 0; s < A_STAGES; ++s) last_issue[s] = -1;
       bool ok = true;
       Item w;
       for (int j = 0; ok && next_item(sched, blockIdx.x, gridDim.x, j, kblocks, num_m, num_n, w);
@@ -352,23 +492,17 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           mbar_arrive_expect_tx(afull(s), L::ACT_BYTES);
           tma_load_2d(act_base + s * L::ACT_BYTES, &act_map, afull(s), kb * BK, mt * TILE_M);
-          last_issue[s] = static_cast<int>(it);
         }
       }
-      if (!ok) {  // let every copy already issued land before the CTA exits
-        volatile int never = 0;
-        for (int s = 0; s < A_STAGES; ++s)
-          if (last_issue[s] >= 0)
-            mbar_wait(afull(s), (static_cast<uint32_t>(last_issue[s]) / A_STAGES) & 1u, &never,
-                      nullptr, 100000000ull);
+      if (!ok) {  // let every copy already issued (the last `it`, at most A_STAGES) land
+        for (uint32_t i = it > A_STAGES ? it - A_STAGES : 0; i < it; ++i)
+          mbar_wait(afull(i % A_STAGES), (i / A_STAGES) & 1u, never, nullptr, 100000000ull);
       }
     }
   } else if (warp == 2) {
     // ----------------------------------------------------- weight producer
     if (lane == 0) {
       uint32_t it = 0;
-      int last_issue[W_STAGES];
-      for (int s = 0; s < W_STAGES; ++s) last_issue[s] = -1;
       bool ok = true;
       Item w;
       for (int j = 0; ok && next_item(sched, blockIdx.x, gridDim.x, j, kblocks, num_m, num_n, w);
@@ -391,15 +525,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                     WBLOCK_BYTES, wfull(s));
           bulk_load(w_base + s * W_SLOT + WBLOCK_BYTES, sblk + static_cast<size_t>(g0) * TILE_N,
                     sbytes, wfull(s));
-          last_issue[s] = static_cast<int>(it);
         }
       }
-      if (!ok) {
-        volatile int never = 0;
-        for (int s = 0; s < W_STAGES; ++s)
-          if (last_issue[s] >= 0)
-            mbar_wait(wfull(s), (static_cast<uint32_t>(last_issue[s]) / W_STAGES) & 1u, &never,
-                      nullptr, 100000000ull);
+      if (!ok) {  // let every copy already issued (the last `it`, at most W_STAGES) land
+        for (uint32_t i = it > W_STAGES ? it - W_STAGES : 0; i < it; ++i)
+          mbar_wait(wfull(i % W_STAGES), (i / W_STAGES) & 1u, never, nullptr, 100000000ull);
       }
     }
   } else if (warp == 1) {
@@ -407,19 +537,37 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       constexpr uint32_t IDESC = idesc_f16_f32(TILE_N, TILE_M);
       uint32_t it = 0, t_local = 0;
+      uint32_t uses0 = 0, uses1 = 0;  // segments committed on accumulator 0 / 1
+      const int promo = sched.promo > 0 ? sched.promo : INT_MAX;
       bool ok = true;
       Item w;
       for (int j = 0; ok && next_item(sched, blockIdx.x, gridDim.x, j, kblocks, num_m, num_n, w);
            ++j, ++t_local) {
         const int acc = t_local % ACC;
-        const uint32_t dph = (t_local / ACC) & 1u;
-        if (!mbar_wait(dempty(acc), dph ^ 1u, abort_flag, status, wait_limit_ns)) {
+        uint32_t uses = acc == 0 ? uses0 : uses1;
+        // the accumulator is free (its last segment drained)
+        if (!mbar_wait(dempty(acc), (uses & 1u) ^ 1u, abort_flag, status, wait_limit_ns)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + ACC_COL0 + acc * TILE_M;
+        int left = promo;
         for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
+          if (left == 0) {
+            // segment boundary: hand the accumulator to the epilogue for
+            // promotion; continue once the remainder is written back
+            tc_commit(dfull(acc));
+            ++uses;
+            if (!mbar_wait_lean(dempty(acc), (uses & 1u) ^ 1u, abort_flag, status,
+                                wait_limit_ns)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            left = promo;
+          }
+          --left;
           const int s = it % A_STAGES;
           const uint32_t ph = (it / A_STAGES) & 1u;
           const int ts = it % T_STAGES;
@@ -435,6 +583,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int k16 = 0; k16 < BK / 16; ++k16) {
             const uint32_t a_tmem = tmem_base + ts * T_COLS + k16 * 8;
             const uint64_t b_desc = smem_desc_sw128(b_addr + k16 * 32);
+            // the item's first MMA starts the sum; later ones (including a
+            // segment's first, onto the promoted remainder) accumulate
             mma_f16_ts(d_tmem, a_tmem, b_desc, IDESC, (kb != w.kb0) || (k16 != 0));
           }
           tc_commit(aempty(s));
@@ -442,11 +592,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         if (!ok) break;
         tc_commit(dfull(acc));
+        ++uses;
+        if (acc == 0) uses0 = uses; else uses1 = uses;
       }
       // Every MMA this thread issued has completed before TMEM is freed.
       tc_commit(drain_bar);
-      volatile int never = 0;
-      mbar_wait(drain_bar, 0, &never, nullptr, 100000000ull);
+      mbar_wait(drain_bar, 0, never, nullptr, 100000000ull);
     }
   } else if (warp < FIRST_EPI_WARP) {
     // ---------------------------------------------------------------- dequant
@@ -504,9 +655,12 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else {
     // --------------------------------------------------------------- epilogue
     // Four warps per lane quarter; warp e covers accumulator columns
-    // [part*TILE_M/4, (part+1)*TILE_M/4) of its 32 lanes. The whole slice is
-    // read into registers before the accumulator is released, so the next
-    // tile's MMAs start while the stores drain.
+    // [part*TILE_M/4, (part+1)*TILE_M/4) of its 32 lanes. At each promotion
+    // boundary of an item the warps fold the accumulator into the running sum
+    // (hb: FP8 high parts, in registers) and write the remainder back. At
+    // the item's end the whole slice (plus hb) is read into registers before
+    // the accumulator is released, so the next tile's MMAs start while the
+    // stores drain.
     constexpr int COLS = TILE_M / 4;
     const int e = warp - FIRST_EPI_WARP;
     const int quarter = warp & 3;
@@ -515,18 +669,47 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     constexpr int EPI_THREADS = NUM_EPI_WARPS * 32;
     uint32_t t_local = 0;
+    uint32_t uses0 = 0, uses1 = 0;  // segments drained from accumulator 0 / 1
     bool failed = false;
     Item w;
     for (int j = 0; next_item(sched, blockIdx.x, gridDim.x, j, kblocks, num_m, num_n, w);
          ++j, ++t_local) {
       const int acc = t_local % ACC;
-      const uint32_t dph = (t_local / ACC) & 1u;
-      const bool ok = !failed && mbar_wait(dfull(acc), dph, abort_flag, status, wait_limit_ns);
+      uint32_t uses = acc == 0 ? uses0 : uses1;
       const uint32_t col0 = tmem_base + lane_addr + ACC_COL0 + acc * TILE_M + half * COLS;
+      const int nblk = w.kb1 - w.kb0;
+      const int nseg = sched.promo > 0 ? (nblk + sched.promo - 1) / sched.promo : 1;
+      uint32_t hb[COLS / 4];  // running sum's high parts (e5m2 x4), zero at the start
+#pragma unroll
+      for (int q = 0; q < COLS / 4; ++q) hb[q] = 0u;
+      for (int sg = 0; sg + 1 < nseg; ++sg, ++uses) {
+        const bool ok = !failed && mbar_wait(dfull(acc), uses & 1u, abort_flag, status,
+                                             wait_limit_ns);
+        if (ok) {
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < COLS / 8; ++c) promote_chunk(col0 + c * 8, &hb[c * 2]);
+          tmem_st_wait();
+        } else {
+          failed = true;
+        }
+        tc_fence_before();
+        mbar_arrive(dempty(acc));
+      }
+      const bool ok = !failed && mbar_wait(dfull(acc), uses & 1u, abort_flag, status,
+                                           wait_limit_ns);
+      ++uses;
+      if (acc == 0) uses0 = uses; else uses1 = uses;
       const int n = w.nt * TILE_N + row;
       const int m0 = w.mt * TILE_M + half * COLS;
       if (w.rem < 0) {
         // ------------------------------------------------ whole tile -> C
+        if constexpr (MULTI) {
+          copies_epilogue<TILE_M>(ok, out, M, w.mt, w.nt, half, row, m0, col0, hb, dempty(acc),
+                                  warp - FIRST_EPI_WARP, lane);
+          if (!ok) failed = true;
+          continue;
+        }
         if (!ok) {
           failed = true;
           continue;
@@ -538,8 +721,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll 1
           for (int c = 0; c < COLS / 16; ++c) {
             uint32_t v[16];
-            tmem_ld_32x32b_x16(col0 + c * 16, v);
-            tmem_ld_wait16(v);
+            load_sum16(col0 + c * 16, hb, v);
+            shift_down4(hb);
             if (c == COLS / 16 - 1) {
               tc_fence_before();
               mbar_arrive(dempty(acc));
@@ -549,13 +732,12 @@ __global__ void __launch_bounds__(THREADS, 1)
               if (m0 + c * 16 + j < M)
                 cp[static_cast<size_t>(c * 16 + j) * N] = __uint_as_float(v[j]);
           }
-        } else if constexpr (!MULTI) {
+        } else {
           uint32_t h[COLS / 2];  // packed halves: h[j] = columns 2j, 2j+1
 #pragma unroll
           for (int c = 0; c < COLS / 16; ++c) {
             uint32_t v[16];
-            tmem_ld_32x32b_x16(col0 + c * 16, v);
-            tmem_ld_wait16(v);
+            load_sum16(col0 + c * 16, &hb[c * 4], v);
             pack_half2(v, &h[c * 8], 8);
           }
           tc_fence_before();
@@ -577,34 +759,6 @@ __global__ void __launch_bounds__(THREADS, 1)
               if (2 * j + 1 < valid) cp[static_cast<size_t>(2 * j + 1) * N] = __high2half(hv);
             }
           }
-        } else {
-          // Several copies of C (this GPU's and peers'): store each 16-column
-          // chunk to every copy as it is read.
-          const size_t ldc = static_cast<size_t>(out.ldc);
-          const size_t off = static_cast<size_t>(m0) * ldc + out.col0 + n;
-#pragma unroll 1
-          for (int c = 0; c < COLS / 16; ++c) {
-            uint32_t v[16];
-            tmem_ld_32x32b_x16(col0 + c * 16, v);
-            tmem_ld_wait16(v);
-            if (c == COLS / 16 - 1) {
-              tc_fence_before();
-              mbar_arrive(dempty(acc));
-            }
-            uint32_t hv[8];
-            pack_half2(v, hv, 8);
-#pragma unroll 1
-            for (int d = 0; d < out.count; ++d) {
-              __half* cp = static_cast<__half*>(out.dst[d]) + off;
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const __half2 p2 = *reinterpret_cast<const __half2*>(&hv[j]);
-                if (m0 + c * 16 + 2 * j < M) cp[(c * 16 + 2 * j) * ldc] = __low2half(p2);
-                if (m0 + c * 16 + 2 * j + 1 < M) cp[(c * 16 + 2 * j + 1) * ldc] = __high2half(p2);
-              }
-            }
-          }
-          __threadfence_system();  // peer copies are read by other GPUs
         }
         continue;
       }
@@ -617,11 +771,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                      static_cast<size_t>(w.slot) * (TILE_M / 4) * TILE_N;
       if (ok) {
         tc_fence_after();
-#pragma unroll 1
+#pragma unroll
         for (int c = 0; c < COLS / 16; ++c) {
           uint32_t v[16];
-          tmem_ld_32x32b_x16(col0 + c * 16, v);
-          tmem_ld_wait16(v);
+          load_sum16(col0 + c * 16, &hb[c * 4], v);
           const int q0 = (half * COLS + c * 16) / 4;
 #pragma unroll
           for (int j = 0; j < 4; ++j)
@@ -680,6 +833,15 @@ __global__ void __launch_bounds__(THREADS, 1)
 // stream-K tail kStreamKUs (two partial items per CTA and up to four partial
 // tiles per output tile).
 constexpr double kBlockUs256 = 0.45, kBlockUs128 = 0.5;
+
+int promote_blocks() {
+  static const int v = [] {
+    const char* e = std::getenv("I4G_PROMOTE_BLOCKS");
+    const int b = e ? std::atoi(e) : 32;
+    return b >= 0 ? b : 32;
+  }();
+  return v;
+}
 constexpr double kSplitUs = 12.0, kStreamKUs = 20.0;
 
 Plan make_plan(int tile_m, int M, int N, int K, int sm_count, size_t budget,
@@ -687,7 +849,8 @@ Plan make_plan(int tile_m, int M, int N, int K, int sm_count, size_t budget,
   Plan p;
   const int tiles = ((M + tile_m - 1) / tile_m) * (N / TILE_N);
   const int kblocks = K / BK;
-  p.sched = Sched{tiles, 1, tiles, 0, 0};
+  const int promo = promote_blocks();
+  p.sched = Sched{tiles, 1, tiles, 0, 0, promo};
   p.grid = tiles < sm_count ? tiles : sm_count;
   p.workspace_bytes = 0;
   if (budget == 0) return p;
@@ -705,7 +868,7 @@ Plan make_plan(int tile_m, int M, int N, int K, int sm_count, size_t budget,
   const size_t split_bytes = kTicketBytes + static_cast<size_t>(rem) * f * tile_bytes;
   if (f >= 2 && split_bytes <= budget && (waves + 1.0 / f) * t_tile + kSplitUs < best) {
     best = (waves + 1.0 / f) * t_tile + kSplitUs;
-    p.sched = Sched{waves * sm_count, f, waves * sm_count + rem * f, 0, 0};
+    p.sched = Sched{waves * sm_count, f, waves * sm_count + rem * f, 0, 0, promo};
     p.grid = p.sched.items < sm_count ? p.sched.items : sm_count;
     p.workspace_bytes = split_bytes;
   }
@@ -726,7 +889,7 @@ Plan make_plan(int tile_m, int M, int N, int K, int sm_count, size_t budget,
     const double sk_time = (waves + static_cast<double>(rem) / chunks) * t_tile + kStreamKUs;
     if (chunks > rem && most <= 4 && run * chunks < (1l << 31) && sk_bytes <= budget &&
         sk_time < best) {
-      p.sched = Sched{waves * sm_count, 1, 0, chunks, rem};
+      p.sched = Sched{waves * sm_count, 1, 0, chunks, rem, promo};
       p.grid = waves > 0 ? sm_count : chunks;
       p.workspace_bytes = sk_bytes;
     }

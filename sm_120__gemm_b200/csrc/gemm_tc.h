@@ -58,9 +58,15 @@ constexpr size_t kTicketBytes = 4096;
 // then the tail. chunks == 0: each of the following tiles split `split` ways
 // along K (items = full_tiles + tail * split). chunks > 0 (stream-K): the
 // `tail_tiles` tiles' blocks cut into `chunks` equal shares, one per CTA.
+// promo > 0: an item's accumulation is cut into segments of `promo` 64-k
+// blocks, each promoted into an FP32 running sum by the epilogue (0: none).
 struct Sched {
-  int full_tiles, split, items, chunks, tail_tiles;
+  int full_tiles, split, items, chunks, tail_tiles, promo;
 };
+
+// 64-k blocks per promotion segment of the tcgen05 kernel (default 32, i.e.
+// 2048 k; I4G_PROMOTE_BLOCKS overrides it, 0 switches promotion off).
+int promote_blocks();
 
 struct Plan {
   Sched sched;
