@@ -29,7 +29,7 @@ __all__ = [
     "gemm_workspace_size", "launch_final_ws", "launch_final_fp32_ws", "workspace_for",
     "launch_final_to_peers", "ipc_handle", "ipc_open", "ipc_close", "peer_barrier",
     "shard_range", "device_status", "selftest_wait_timeout", "plan", "set_decode_schedule",
-    "kernel_config", "kernel_resources",
+    "kernel_config", "kernel_resources", "max_pairs",
     "QuantizedLinear", "VARIANT_AUTO", "VARIANT_TC", "VARIANT_DECODE", "DECODE_SCHEDULES",
     "PLAN_KERNELS", "PLAN_SCHEDULES", "LIB_PATH",
 ]
@@ -99,6 +99,7 @@ class _KernelResources(ctypes.Structure):
 
 
 _SIGNATURES["i4g_kernel_config"] = [_i, _i, _i, ctypes.POINTER(_KernelConfig)]
+_SIGNATURES["i4g_max_pairs"] = [ctypes.POINTER(_i)]
 _SIGNATURES["i4g_kernel_resources"] = [_i, _i, _i, ctypes.POINTER(_KernelResources)]
 
 
@@ -371,6 +372,14 @@ def kernel_resources(variant: int, rows: int, group: int) -> dict:
     r = _KernelResources()
     _call("i4g_kernel_resources", variant, rows, group, ctypes.byref(r))
     return {n: getattr(r, n) for n, _ in _KernelResources._fields_}
+
+
+def max_pairs() -> int:
+    """C ABI i4g_max_pairs: CTA pairs of the paired tcgen05 kernel resident at
+    once on the current device."""
+    v = _i()
+    _call("i4g_max_pairs", ctypes.byref(v))
+    return v.value
 
 
 DECODE_SCHEDULES = {"auto": 0, "cluster": 1, "streamk": 2}

@@ -290,9 +290,11 @@ int gemm_common(const void* A, const uint8_t* tiles, const void* scales, const i
   }
   const int tile_m = tc_tile_m(M, N, dev);
   const i4g::tc::Plan plan = i4g::tc::make_plan(tile_m, M, N, K, dev->sm_count,
-                                                workspace ? workspace_bytes : 0, true);
+                                                workspace ? workspace_bytes : 0, true,
+                                                i4g::tc::max_pairs(dev->sm_count));
   const CUtensorMap* map = nullptr;
-  st = act_map(A, M, K, tile_m, &map);
+  // each CTA of a pair loads half of the tile's activation rows
+  st = act_map(A, M, K, tile_m / plan.cg, &map);
   if (st != I4G_OK) return st;
   return finish(i4g::tc::launch(*map, tile_m, tiles, sc, out, fp32_out, M, N, K, group, plan,
                                 plan.workspace_bytes > 0 ? workspace : nullptr,
@@ -550,7 +552,8 @@ int i4g_gemm_workspace_size(int M, int N, int K, size_t* bytes) {
   if (st != I4G_OK) return st;
   DeviceInfo* dev = nullptr;
   if ((st = current_device(&dev)) != I4G_OK) return st;
-  *bytes = i4g::tc::make_plan(tc_tile_m(M, N, dev), M, N, K, dev->sm_count, SIZE_MAX, true)
+  *bytes = i4g::tc::make_plan(tc_tile_m(M, N, dev), M, N, K, dev->sm_count, SIZE_MAX, true,
+                              i4g::tc::max_pairs(dev->sm_count))
                .workspace_bytes;
   if (i4g::dec::supported(M, K, 32)) {  // FP16 C at these M runs the decode kernel
     const i4g::dec::SkPlan sk = i4g::dec::sk_plan(M, N, K, dev->sm_count);
@@ -580,7 +583,8 @@ int i4g_gemm_static_scratch(const void* A, const uint8_t* tiles, const void* sca
   if ((st = current_device(&dev)) != I4G_OK) return st;
   size_t need = 0;
   if (!i4g::dec::supported(M, K, group)) {
-    need = i4g::tc::make_plan(tc_tile_m(M, N, dev), M, N, K, dev->sm_count, SIZE_MAX, true)
+    need = i4g::tc::make_plan(tc_tile_m(M, N, dev), M, N, K, dev->sm_count, SIZE_MAX, true,
+                              i4g::tc::max_pairs(dev->sm_count))
                .workspace_bytes;
   } else {
     // the decode kernel's stream-K schedule when its workspace fits the
@@ -773,6 +777,15 @@ int i4g_kernel_resources(int variant, int rows, int group, i4g_kernel_resources_
                                                   : i4g::dec::resources(rows, group, &r);
   if (e != cudaSuccess) return record_cuda(e, "kernel attribute query");
   *out = i4g_kernel_resources_t{r.registers, r.static_smem, r.max_threads, r.active_per_sm};
+  return I4G_OK;
+}
+
+int i4g_max_pairs(int* pairs) {
+  if (!pairs) return fail(I4G_ERR_NULL_POINTER, "null pointer argument");
+  DeviceInfo* dev = nullptr;
+  const int st = current_device(&dev);
+  if (st != I4G_OK) return st;
+  *pairs = i4g::tc::max_pairs(dev->sm_count);
   return I4G_OK;
 }
 

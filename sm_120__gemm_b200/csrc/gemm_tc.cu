@@ -68,12 +68,15 @@ constexpr int TILE_N = 128;         // weight columns per tile (MMA-M)
 constexpr int BK = 64;              // k per stage (one 128-byte swizzle row)
 constexpr int T_COLS = 32;          // TMEM columns per dequantised weight stage (64 halves)
 constexpr int T_STAGES = 8;         // TMEM weight stages
-constexpr int DEQ_GROUPS = 2;       // dequant warp groups (4 warps = 128 lanes each)
+constexpr int DEQ_GROUPS = 1;       // dequant warp groups (4 warps = 128 lanes each)
 constexpr int NUM_DEQ_WARPS = 4 * DEQ_GROUPS;
 constexpr int NUM_EPI_WARPS = 16;   // four per TMEM lane quarter
 constexpr int FIRST_DEQ_WARP = 3;
 constexpr int FIRST_EPI_WARP = FIRST_DEQ_WARP + NUM_DEQ_WARPS;
 constexpr int THREADS = 32 * (FIRST_EPI_WARP + NUM_EPI_WARPS);
+// 23 warps (736 threads): 88 registers a thread
+static_assert(NUM_DEQ_WARPS == 4 && NUM_EPI_WARPS == 16, "each TMEM lane quarter (warp % 4) "
+              "has one dequant warp and four epilogue warps");
 constexpr int TMEM_COLS = 512;
 constexpr int ACC_COL0 = T_STAGES * T_COLS;    // 256
 constexpr int WBLOCK_BYTES = TILE_N * BK / 2;  // 4096: one tile-layout block
@@ -82,11 +85,14 @@ constexpr int W_SLOT = WBLOCK_BYTES + SCALE_BYTES;
 constexpr int W_STAGES = 8;
 constexpr int GROUP_M = 8;                     // rasterisation band (m-tiles)
 
-template <int TILE_M>
+// CG = 1: one CTA per tile. CG = 2: a CTA pair (cluster of two) per tile of
+// 2 x 128 weight columns, each CTA loading half of the TILE_M activation rows.
+template <int TILE_M, int CG>
 struct Cfg {
   static constexpr int ACC = TILE_M <= 128 ? 2 : 1;  // accumulators in TMEM
-  static constexpr int ACT_BYTES = TILE_M * BK * 2;
-  static constexpr int A_STAGES = TILE_M <= 128 ? 8 : 5;
+  static constexpr int ROWS = TILE_M / CG;           // activation rows this CTA loads
+  static constexpr int ACT_BYTES = ROWS * BK * 2;
+  static constexpr int A_STAGES = (CG == 2 || TILE_M <= 128) ? 8 : 5;
   static constexpr int ACT_OFF = 0;
   static constexpr int W_OFF = ACT_OFF + A_STAGES * ACT_BYTES;
   static constexpr int BAR_OFF = W_OFF + W_STAGES * W_SLOT;
@@ -183,13 +189,14 @@ __device__ __forceinline__ bool next_item(const Sched& s, int b, int g, int j, i
 // Sums SPLIT partial tiles in split order (a fixed order, so results do not
 // depend on which CTA finished last) and writes quads*4 rows of column n of C,
 // starting at row m0. `base` points at this thread's first quad of split 0;
-// quads of one split are TILE_N float4 apart, splits (TILE_M/4)*TILE_N.
+// quads of one split are TILE_N float4 apart, splits CG*(TILE_M/4)*TILE_N.
 // B quads are loaded for every split before any is summed, to overlap the
 // L2 latency.
-template <int TILE_M, int SPLIT, int B, bool FP32_OUT, bool MULTI>
+template <int TILE_M, int SPLIT, int B, bool FP32_OUT, bool MULTI, int CG>
 __device__ __forceinline__ void reduce_partials(const float4* base, const Outputs& out, int m0,
                                                 int n, int M, int N, int quads) {
-  constexpr size_t kSplitStride = static_cast<size_t>(TILE_M / 4) * TILE_N;
+  // a pair's two halves interleave their slots
+  constexpr size_t kSplitStride = static_cast<size_t>(CG) * (TILE_M / 4) * TILE_N;
 #pragma unroll 1
   for (int q = 0; q < quads; q += B) {
     float4 t[SPLIT][B];
@@ -229,15 +236,6 @@ __device__ __forceinline__ void reduce_partials(const float4* base, const Output
     }
   }
   if constexpr (MULTI) __threadfence_system();  // peer copies are read by other GPUs
-}
-
-// Convert 32 fp32 accumulator columns of one lane into 16 packed halves.
-__device__ __forceinline__ void pack_half2(const uint32_t* v, uint32_t* out, int n) {
-#pragma unroll
-  for (int j = 0; j < n; ++j) {
-    const __half2 h = __floats2half2_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
-    out[j] = *reinterpret_cast<const uint32_t*>(&h);
-  }
 }
 
 __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
@@ -336,7 +334,7 @@ __device__ __forceinline__ void shift_down4(uint32_t (&hb)[NW]) {
 // 16-byte pieces, so the NVLink traffic moves in full 16-byte stores and the
 // next tile's MMAs never wait on it. Every epilogue thread takes the barrier
 // whatever `ok` is (a failed wait skips the work, never the barrier).
-template <int TILE_M>
+template <int TILE_M, int CG>
 __device__ __forceinline__ void copies_epilogue(bool ok, const Outputs& out, int M, int mt, int nt,
                                              int half, int row, int m0, uint32_t col0,
                                              const uint32_t* hb, uint32_t empty_bar, int epi_warp,
@@ -348,24 +346,24 @@ __device__ __forceinline__ void copies_epilogue(bool ok, const Outputs& out, int
   __half* const tile0 = static_cast<__half*>(out.dst[0]) + tile_off;
   if (ok) {
     tc_fence_after();
-    uint32_t h[COLS / 2];  // packed halves: h[j] = columns 2j, 2j+1
+    // each 16-column chunk is stored into this GPU's copy as it is read; the
+    // accumulator is released once the last chunk is in registers
+    __half* cp = tile0 + static_cast<size_t>(half * COLS) * ldc + row;
+    const int valid = min(COLS, M - m0);
 #pragma unroll
     for (int c = 0; c < COLS / 16; ++c) {
       uint32_t v[16];
       load_sum16(col0 + c * 16, &hb[c * 4], v);
-      pack_half2(v, &h[c * 8], 8);
-    }
-    tc_fence_before();
-    mbar_arrive(empty_bar);
-    __half* cp = tile0 + static_cast<size_t>(half * COLS) * ldc + row;
-    const int valid = min(COLS, M - m0);
+      if (c == COLS / 16 - 1) {
+        tc_fence_before();
+        if constexpr (CG == 2) mbar_arrive_cluster(empty_bar);  // the even CTA's barrier
+        else mbar_arrive(empty_bar);
+      }
 #pragma unroll
-    for (int j = 0; j < COLS / 2; ++j) {
-      const __half2 p2 = *reinterpret_cast<const __half2*>(&h[j]);
-      if (2 * j < valid) *cp = __low2half(p2);
-      cp += ldc;
-      if (2 * j + 1 < valid) *cp = __high2half(p2);
-      cp += ldc;
+      for (int j = 0; j < 16; ++j) {
+        if (c * 16 + j < valid) *cp = __float2half_rn(__uint_as_float(v[j]));
+        cp += ldc;
+      }
     }
   }
   if (out.count == 1) return;
@@ -385,6 +383,18 @@ __device__ __forceinline__ void copies_epilogue(bool ok, const Outputs& out, int
   __threadfence_system();  // peer copies are read by other GPUs
 }
 
+// Rotates a running-sum array down by two words (the first two move to the
+// end), so that a rolled loop over 8-column chunks always updates words 0, 1
+// and a full pass leaves the array in its original order.
+template <int NW>
+__device__ __forceinline__ void rotate_down2(uint32_t (&hb)[NW]) {
+  const uint32_t w0 = hb[0], w1 = hb[1];
+#pragma unroll
+  for (int q = 0; q + 2 < NW; ++q) hb[q] = hb[q + 2];
+  hb[NW - 2] = w0;
+  hb[NW - 1] = w1;
+}
+
 // OUT selects the C epilogue at compile time, so the plain kernels carry no
 // code for the general one: half C or float C as one row-major [M][N] matrix
 // (out.dst[0]; ldc == N, col0 == 0), or half C written to columns
@@ -392,18 +402,19 @@ __device__ __forceinline__ void copies_epilogue(bool ok, const Outputs& out, int
 // peers').
 enum OutKind : int { kOutHalf = 0, kOutFloat = 1, kOutHalfCopies = 2 };
 
-template <int TILE_M, int GROUP, int OUT>
+template <int TILE_M, int GROUP, int OUT, int CG>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap act_map,
                    const uint8_t* __restrict__ tiles, const __half* __restrict__ scales,
                    const __grid_constant__ Outputs out, int M, int N, int K, const Sched sched,
                    uint32_t* __restrict__ tickets, float* __restrict__ partials, int* status,
                    unsigned long long wait_limit_ns) {
-  using L = Cfg<TILE_M>;
+  using L = Cfg<TILE_M, CG>;
   constexpr int A_STAGES = L::A_STAGES;
   constexpr int ACC = L::ACC;
   constexpr bool FP32_OUT = OUT == kOutFloat;
   constexpr bool MULTI = OUT == kOutHalfCopies;
+  constexpr bool PAIR = CG == 2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -436,14 +447,29 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // CTA pairs: the even CTA (rank 0) issues the pair's MMAs; both CTAs load
+  // their own half of the activation rows, dequantise their own 128 weight
+  // columns into their own TMEM and drain their own accumulator. Barriers
+  // the MMA waits on (afull, tfull, dempty) live in the even CTA and count
+  // both CTAs' arrivals; the MMA's completions (aempty, tempty, dfull, drain)
+  // arrive in both CTAs at once (multicast commit).
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;
+  const bool leader = rank == 0;
+  const int unit = blockIdx.x / CG, units = gridDim.x / CG;  // work is handed out per pair
   const int num_m = (M + TILE_M - 1) / TILE_M;
-  const int num_n = N / TILE_N;
+  const int num_n = N / (TILE_N * CG);
   const int kblocks = K / BK;
   const int groups = K / GROUP;
+  // the even CTA's copy of a barrier (for arrivals from the odd CTA): the
+  // shared::cluster window of a CTA is linear, so one mapa serves them all
+  const uint32_t lead_bar_base = PAIR ? mapa_shared(bar_base, 0) : bar_base;
+  auto lead = [&](uint32_t bar) { return lead_bar_base + (bar - bar_base); };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < A_STAGES; ++i) {
-      mbar_init(afull(i), 1);
+      // own producer's expected bytes; in the even CTA of a pair also the odd
+      // CTA's relay (its half landed)
+      mbar_init(afull(i), PAIR && leader ? 2 : 1);
       mbar_init(aempty(i), 1);  // MMA completion
     }
     for (int i = 0; i < W_STAGES; ++i) {
@@ -451,12 +477,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(wempty(i), 4);  // the four warps of the dequant group that read it
     }
     for (int i = 0; i < T_STAGES; ++i) {
-      mbar_init(tfull(i), 4 * 32);
-      mbar_init(tempty(i), 1);  // MMA completion
+      mbar_init(tfull(i), CG * 4 * 32);  // the dequant threads of both CTAs of a pair
+      mbar_init(tempty(i), 1);           // MMA completion
     }
     for (int i = 0; i < ACC; ++i) {
       mbar_init(dfull(i), 1);
-      mbar_init(dempty(i), NUM_EPI_WARPS * 32);
+      mbar_init(dempty(i), CG * NUM_EPI_WARPS * 32);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -466,11 +492,18 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
   if (warp == 0 && lane == 0) prefetch_tensormap(&act_map);
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(smem_u32(tmem_slot), TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  // a pair's barriers are initialised before either CTA arrives on the other's
+  if constexpr (PAIR) cluster_barrier();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -480,18 +513,21 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t it = 0;
       bool ok = true;
       Item w;
-      for (int j = 0; ok && next_item(sched, blockIdx.x, gridDim.x, j, kblocks, num_m, num_n, w);
-           ++j) {
-        const int mt = w.mt;
+      for (int j = 0; ok && next_item(sched, unit, units, j, kblocks, num_m, num_n, w); ++j) {
+        const int row0 = w.mt * TILE_M + static_cast<int>(rank) * L::ROWS;
         for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
           const int s = it % A_STAGES;
           const uint32_t ph = (it / A_STAGES) & 1u;
-          if (!mbar_wait(aempty(s), ph ^ 1u, abort_flag, status, wait_limit_ns)) {
+          const bool free = PAIR ? mbar_wait_cluster(aempty(s), ph ^ 1u, abort_flag, status,
+                                                     wait_limit_ns)
+                                 : mbar_wait(aempty(s), ph ^ 1u, abort_flag, status,
+                                             wait_limit_ns);
+          if (!free) {
             ok = false;
             break;
           }
           mbar_arrive_expect_tx(afull(s), L::ACT_BYTES);
-          tma_load_2d(act_base + s * L::ACT_BYTES, &act_map, afull(s), kb * BK, mt * TILE_M);
+          tma_load_2d(act_base + s * L::ACT_BYTES, &act_map, afull(s), kb * BK, row0);
         }
       }
       if (!ok) {  // let every copy already issued (the last `it`, at most A_STAGES) land
@@ -505,10 +541,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t it = 0;
       bool ok = true;
       Item w;
-      for (int j = 0; ok && next_item(sched, blockIdx.x, gridDim.x, j, kblocks, num_m, num_n, w);
-           ++j) {
-        const uint8_t* wblk = tiles + static_cast<size_t>(w.nt) * kblocks * WBLOCK_BYTES;
-        const __half* sblk = scales + static_cast<size_t>(w.nt) * groups * TILE_N;
+      for (int j = 0; ok && next_item(sched, unit, units, j, kblocks, num_m, num_n, w); ++j) {
+        const int nt = w.nt * CG + static_cast<int>(rank);
+        const uint8_t* wblk = tiles + static_cast<size_t>(nt) * kblocks * WBLOCK_BYTES;
+        const __half* sblk = scales + static_cast<size_t>(nt) * groups * TILE_N;
         for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
           const int s = it % W_STAGES;
           const uint32_t ph = (it / W_STAGES) & 1u;
@@ -534,19 +570,28 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------- MMA issue
-    if (lane == 0) {
-      constexpr uint32_t IDESC = idesc_f16_f32(TILE_N, TILE_M);
+    if (lane == 0 && leader) {
+      // pair: MMA-M 256 (128 weight columns from each CTA's TMEM)
+      constexpr uint32_t IDESC = idesc_f16_f32(TILE_N * CG, TILE_M);
       uint32_t it = 0, t_local = 0;
       uint32_t uses0 = 0, uses1 = 0;  // segments committed on accumulator 0 / 1
       const int promo = sched.promo > 0 ? sched.promo : INT_MAX;
       bool ok = true;
+      auto wait_in = [&](uint32_t bar, uint32_t parity) {
+        return PAIR ? mbar_wait_cluster(bar, parity, abort_flag, status, wait_limit_ns)
+                    : mbar_wait_lean(bar, parity, abort_flag, status, wait_limit_ns);
+      };
+      auto commit = [&](uint32_t bar) {
+        if constexpr (PAIR) tc_commit_pair(bar);
+        else tc_commit(bar);
+      };
       Item w;
-      for (int j = 0; ok && next_item(sched, blockIdx.x, gridDim.x, j, kblocks, num_m, num_n, w);
+      for (int j = 0; ok && next_item(sched, unit, units, j, kblocks, num_m, num_n, w);
            ++j, ++t_local) {
         const int acc = t_local % ACC;
         uint32_t uses = acc == 0 ? uses0 : uses1;
         // the accumulator is free (its last segment drained)
-        if (!mbar_wait(dempty(acc), (uses & 1u) ^ 1u, abort_flag, status, wait_limit_ns)) {
+        if (!wait_in(dempty(acc), (uses & 1u) ^ 1u)) {
           ok = false;
           break;
         }
@@ -557,10 +602,9 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (left == 0) {
             // segment boundary: hand the accumulator to the epilogue for
             // promotion; continue once the remainder is written back
-            tc_commit(dfull(acc));
+            commit(dfull(acc));
             ++uses;
-            if (!mbar_wait_lean(dempty(acc), (uses & 1u) ^ 1u, abort_flag, status,
-                                wait_limit_ns)) {
+            if (!wait_in(dempty(acc), (uses & 1u) ^ 1u)) {
               ok = false;
               break;
             }
@@ -572,8 +616,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t ph = (it / A_STAGES) & 1u;
           const int ts = it % T_STAGES;
           const uint32_t tph = (it / T_STAGES) & 1u;
-          if (!mbar_wait_lean(afull(s), ph, abort_flag, status, wait_limit_ns) ||
-              !mbar_wait_lean(tfull(ts), tph, abort_flag, status, wait_limit_ns)) {
+          if (!wait_in(afull(s), ph) || !wait_in(tfull(ts), tph)) {
             ok = false;
             break;
           }
@@ -585,30 +628,46 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint64_t b_desc = smem_desc_sw128(b_addr + k16 * 32);
             // the item's first MMA starts the sum; later ones (including a
             // segment's first, onto the promoted remainder) accumulate
-            mma_f16_ts(d_tmem, a_tmem, b_desc, IDESC, (kb != w.kb0) || (k16 != 0));
+            const uint32_t accumulate = (kb != w.kb0) || (k16 != 0);
+            if constexpr (PAIR) mma_f16_ts_pair(d_tmem, a_tmem, b_desc, IDESC, accumulate);
+            else mma_f16_ts(d_tmem, a_tmem, b_desc, IDESC, accumulate);
           }
-          tc_commit(aempty(s));
-          tc_commit(tempty(ts));
+          commit(aempty(s));
+          commit(tempty(ts));
         }
         if (!ok) break;
-        tc_commit(dfull(acc));
+        commit(dfull(acc));
         ++uses;
         if (acc == 0) uses0 = uses; else uses1 = uses;
       }
-      // Every MMA this thread issued has completed before TMEM is freed.
-      tc_commit(drain_bar);
-      mbar_wait(drain_bar, 0, never, nullptr, 100000000ull);
+      // Every MMA this thread issued has completed before TMEM is freed (in
+      // both CTAs of a pair: the commit arrives in each).
+      commit(drain_bar);
     }
+    if (PAIR && !leader && lane == 0) {
+      // odd CTA of a pair: its activation half landed -> tell the even CTA,
+      // whose MMAs read it
+      uint32_t total = 0;
+      Item w;
+      for (int j = 0; next_item(sched, unit, units, j, kblocks, num_m, num_n, w); ++j)
+        total += static_cast<uint32_t>(w.kb1 - w.kb0);
+      for (uint32_t it = 0; it < total; ++it) {
+        const int s = it % A_STAGES;
+        if (!mbar_wait(afull(s), (it / A_STAGES) & 1u, abort_flag, status, wait_limit_ns)) break;
+        mbar_arrive_cluster(lead(afull(s)));
+      }
+    }
+    if (lane == 0) mbar_wait(drain_bar, 0, never, nullptr, 100000000ull);
   } else if (warp < FIRST_EPI_WARP) {
     // ---------------------------------------------------------------- dequant
-    const int dgroup = (warp - FIRST_DEQ_WARP) >> 2;
+    const int dgroup = (warp - FIRST_DEQ_WARP) >> 2;  // 0 (one group of four warps)
     const int quarter = warp & 3;          // TMEM lanes this warp may access
     const int row = quarter * 32 + lane;   // weight column inside the tile
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     uint32_t it = static_cast<uint32_t>(dgroup);
     uint32_t total = 0;  // 64-k blocks this CTA processes, over all its items
     Item w;
-    for (int j = 0; next_item(sched, blockIdx.x, gridDim.x, j, kblocks, num_m, num_n, w); ++j) {
+    for (int j = 0; next_item(sched, unit, units, j, kblocks, num_m, num_n, w); ++j) {
       total += static_cast<uint32_t>(w.kb1 - w.kb0);
     }
     for (; it < total; it += DEQ_GROUPS) {
@@ -645,12 +704,16 @@ __global__ void __launch_bounds__(THREADS, 1)
         r[4 * i + 2] = decode_pair<2>(wv[i], sc);
         r[4 * i + 3] = decode_pair<3>(wv[i], sc);
       }
-      if (!mbar_wait(tempty(ts), tph ^ 1u, abort_flag, status, wait_limit_ns)) break;
+      const bool free = PAIR ? mbar_wait_cluster(tempty(ts), tph ^ 1u, abort_flag, status,
+                                                 wait_limit_ns)
+                             : mbar_wait(tempty(ts), tph ^ 1u, abort_flag, status, wait_limit_ns);
+      if (!free) break;
       tc_fence_after();
       tmem_st_32x32b_x32(tmem_base + lane_addr + ts * T_COLS, r);
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(tfull(ts));
+      if constexpr (PAIR) mbar_arrive_cluster(lead(tfull(ts)));
+      else mbar_arrive(tfull(ts));
     }
   } else {
     // --------------------------------------------------------------- epilogue
@@ -660,7 +723,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // (hb: FP8 high parts, in registers) and write the remainder back. At
     // the item's end the whole slice (plus hb) is read into registers before
     // the accumulator is released, so the next tile's MMAs start while the
-    // stores drain.
+    // stores drain. A pair's epilogues release into the even CTA's barrier.
     constexpr int COLS = TILE_M / 4;
     const int e = warp - FIRST_EPI_WARP;
     const int quarter = warp & 3;
@@ -668,12 +731,19 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int row = quarter * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     constexpr int EPI_THREADS = NUM_EPI_WARPS * 32;
+    auto release = [&](int acc) {
+      if constexpr (PAIR) mbar_arrive_cluster(lead(dempty(acc)));
+      else mbar_arrive(dempty(acc));
+    };
+    auto wait_full = [&](int acc, uint32_t parity) {
+      return PAIR ? mbar_wait_cluster(dfull(acc), parity, abort_flag, status, wait_limit_ns)
+                  : mbar_wait(dfull(acc), parity, abort_flag, status, wait_limit_ns);
+    };
     uint32_t t_local = 0;
     uint32_t uses0 = 0, uses1 = 0;  // segments drained from accumulator 0 / 1
     bool failed = false;
     Item w;
-    for (int j = 0; next_item(sched, blockIdx.x, gridDim.x, j, kblocks, num_m, num_n, w);
-         ++j, ++t_local) {
+    for (int j = 0; next_item(sched, unit, units, j, kblocks, num_m, num_n, w); ++j, ++t_local) {
       const int acc = t_local % ACC;
       uint32_t uses = acc == 0 ? uses0 : uses1;
       const uint32_t col0 = tmem_base + lane_addr + ACC_COL0 + acc * TILE_M + half * COLS;
@@ -683,30 +753,32 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
       for (int q = 0; q < COLS / 4; ++q) hb[q] = 0u;
       for (int sg = 0; sg + 1 < nseg; ++sg, ++uses) {
-        const bool ok = !failed && mbar_wait(dfull(acc), uses & 1u, abort_flag, status,
-                                             wait_limit_ns);
+        const bool ok = !failed && wait_full(acc, uses & 1u);
         if (ok) {
           tc_fence_after();
-#pragma unroll
-          for (int c = 0; c < COLS / 8; ++c) promote_chunk(col0 + c * 8, &hb[c * 2]);
+#pragma unroll 1
+          for (int c = 0; c < COLS / 8; ++c) {
+            promote_chunk(col0 + c * 8, hb);
+            rotate_down2(hb);
+          }
           tmem_st_wait();
         } else {
           failed = true;
         }
         tc_fence_before();
-        mbar_arrive(dempty(acc));
+        release(acc);
       }
-      const bool ok = !failed && mbar_wait(dfull(acc), uses & 1u, abort_flag, status,
-                                           wait_limit_ns);
+      const bool ok = !failed && wait_full(acc, uses & 1u);
       ++uses;
       if (acc == 0) uses0 = uses; else uses1 = uses;
-      const int n = w.nt * TILE_N + row;
+      const int nt = w.nt * CG + static_cast<int>(rank);  // this CTA's 128 columns
+      const int n = nt * TILE_N + row;
       const int m0 = w.mt * TILE_M + half * COLS;
       if (w.rem < 0) {
         // ------------------------------------------------ whole tile -> C
         if constexpr (MULTI) {
-          copies_epilogue<TILE_M>(ok, out, M, w.mt, w.nt, half, row, m0, col0, hb, dempty(acc),
-                                  warp - FIRST_EPI_WARP, lane);
+          copies_epilogue<TILE_M, CG>(ok, out, M, w.mt, nt, half, row, m0, col0, hb,
+                                      lead(dempty(acc)), warp - FIRST_EPI_WARP, lane);
           if (!ok) failed = true;
           continue;
         }
@@ -725,7 +797,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             shift_down4(hb);
             if (c == COLS / 16 - 1) {
               tc_fence_before();
-              mbar_arrive(dempty(acc));
+              release(acc);
             }
 #pragma unroll
             for (int j = 0; j < 16; ++j)
@@ -733,30 +805,22 @@ __global__ void __launch_bounds__(THREADS, 1)
                 cp[static_cast<size_t>(c * 16 + j) * N] = __uint_as_float(v[j]);
           }
         } else {
-          uint32_t h[COLS / 2];  // packed halves: h[j] = columns 2j, 2j+1
+          // each 16-column chunk is stored as it is read; the accumulator
+          // is released once the last chunk is in registers
+          __half* cp = static_cast<__half*>(out.dst[0]) + static_cast<size_t>(m0) * N + n;
+          const int valid = min(COLS, M - m0);
 #pragma unroll
           for (int c = 0; c < COLS / 16; ++c) {
             uint32_t v[16];
             load_sum16(col0 + c * 16, &hb[c * 4], v);
-            pack_half2(v, &h[c * 8], 8);
-          }
-          tc_fence_before();
-          mbar_arrive(dempty(acc));
-          __half* cp = static_cast<__half*>(out.dst[0]) + static_cast<size_t>(m0) * N + n;
-          const int valid = min(COLS, M - m0);
-          if (valid >= COLS) {
-#pragma unroll
-            for (int j = 0; j < COLS / 2; ++j) {
-              const __half2 hv = *reinterpret_cast<const __half2*>(&h[j]);
-              cp[static_cast<size_t>(2 * j) * N] = __low2half(hv);
-              cp[static_cast<size_t>(2 * j + 1) * N] = __high2half(hv);
+            if (c == COLS / 16 - 1) {
+              tc_fence_before();
+              release(acc);
             }
-          } else {
 #pragma unroll
-            for (int j = 0; j < COLS / 2; ++j) {
-              const __half2 hv = *reinterpret_cast<const __half2*>(&h[j]);
-              if (2 * j < valid) cp[static_cast<size_t>(2 * j) * N] = __low2half(hv);
-              if (2 * j + 1 < valid) cp[static_cast<size_t>(2 * j + 1) * N] = __high2half(hv);
+            for (int j = 0; j < 16; ++j) {
+              if (c * 16 + j < valid) *cp = __float2half_rn(__uint_as_float(v[j]));
+              cp += N;
             }
           }
         }
@@ -766,9 +830,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       // Every epilogue warp takes the same barriers below whatever happened,
       // so a failed wait cannot strand the others at a barrier. A partial
       // tile is stored as float4 quads [m / 4][n][m % 4], so that each warp
-      // access is 512 contiguous bytes.
+      // access is 512 contiguous bytes. The two CTAs of a pair use their own
+      // slots (slot * CG + rank) and tickets (tile * CG + rank).
       float4* mine = reinterpret_cast<float4*>(partials) +
-                     static_cast<size_t>(w.slot) * (TILE_M / 4) * TILE_N;
+                     static_cast<size_t>(w.slot * CG + static_cast<int>(rank)) * (TILE_M / 4) *
+                         TILE_N;
       if (ok) {
         tc_fence_after();
 #pragma unroll
@@ -783,45 +849,51 @@ __global__ void __launch_bounds__(THREADS, 1)
                                __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3])));
         }
         tc_fence_before();
-        mbar_arrive(dempty(acc));
+        release(acc);
         __threadfence();
       }
       if (!epi_bar_and(EPI_THREADS, ok)) {
         failed = true;
         continue;
       }
-      if (warp == FIRST_EPI_WARP && lane == 0) *ticket_slot = atomicAdd(&tickets[w.rem], 1u);
+      const int ticket = w.rem * CG + static_cast<int>(rank);
+      if (warp == FIRST_EPI_WARP && lane == 0) *ticket_slot = atomicAdd(&tickets[ticket], 1u);
       epi_bar_sync(EPI_THREADS);
       const bool last = *ticket_slot == static_cast<uint32_t>(w.nparts - 1);
       if (last) {
         __threadfence();
         const float4* base = reinterpret_cast<const float4*>(partials) +
-                             static_cast<size_t>(w.base_slot) * (TILE_M / 4) * TILE_N +
+                             static_cast<size_t>(w.base_slot * CG + static_cast<int>(rank)) *
+                                 (TILE_M / 4) * TILE_N +
                              static_cast<size_t>(half * COLS / 4) * TILE_N + row;
         const int mq = w.mt * TILE_M + half * COLS;
         switch (w.nparts) {
           case 2:
-            reduce_partials<TILE_M, 2, 4, FP32_OUT, MULTI>(base, out, mq, n, M, N, COLS / 4);
+            reduce_partials<TILE_M, 2, 4, FP32_OUT, MULTI, CG>(base, out, mq, n, M, N, COLS / 4);
             break;
           case 3:
-            reduce_partials<TILE_M, 3, 2, FP32_OUT, MULTI>(base, out, mq, n, M, N, COLS / 4);
+            reduce_partials<TILE_M, 3, 2, FP32_OUT, MULTI, CG>(base, out, mq, n, M, N, COLS / 4);
             break;
           default:
-            reduce_partials<TILE_M, 4, 2, FP32_OUT, MULTI>(base, out, mq, n, M, N, COLS / 4);
+            reduce_partials<TILE_M, 4, 2, FP32_OUT, MULTI, CG>(base, out, mq, n, M, N, COLS / 4);
             break;
         }
       }
       epi_bar_sync(EPI_THREADS);  // the ticket slot is read by all before it changes
-      if (last && warp == FIRST_EPI_WARP && lane == 0) tickets[w.rem] = 0u;
+      if (last && warp == FIRST_EPI_WARP && lane == 0) tickets[ticket] = 0u;
     }
   }
 
   __syncwarp();
   tc_fence_before();
   __syncthreads();
+  // neither CTA of a pair leaves (or frees TMEM) while the other may still
+  // arrive on its barriers or its MMAs run on its TMEM
+  if constexpr (PAIR) cluster_barrier();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
@@ -844,39 +916,92 @@ int promote_blocks() {
 }
 constexpr double kSplitUs = 12.0, kStreamKUs = 20.0;
 
+int pair_mode() {
+  static const int v = [] {
+    const char* e = std::getenv("I4G_PAIR");
+    return e ? std::atoi(e) : 1;
+  }();
+  return v;
+}
+
+int choose_cg(int tile_m, int N, int sm_count) {
+  // CTA pairs for the 256-row tiles when the weight columns split into
+  // 256-column pair tiles (I4G_PAIR=0 keeps single CTAs).
+  return (pair_mode() != 0 && tile_m == 256 && N % 256 == 0 && sm_count >= 2) ? 2 : 1;
+}
+
+int max_pairs(int sm_count) {
+  // CTA pairs that can be resident at once (clusters are placed within GPCs,
+  // so this can be fewer than sm_count / 2); per device, asked once.
+  constexpr int kDevices = 64;
+  static std::atomic<int> cached[kDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kDevices) return sm_count / 2;
+  int v = cached[dev].load(std::memory_order_relaxed);
+  if (v > 0) return v;
+  auto kernel = gemm_tc_kernel<256, 128, kOutHalf, 2>;
+  using L = Cfg<256, 2>;
+  static std::atomic<uint64_t> configured{0};
+  int n = 0;
+  if (ensure_dynamic_smem(kernel, L::DYN_BYTES, configured) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (sm_count / 2));
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = L::DYN_BYTES;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) n = 0;
+  }
+  cudaGetLastError();  // a failed query leaves no error behind
+  v = (n > 0 && n < sm_count / 2) ? n : sm_count / 2;
+  cached[dev].store(v, std::memory_order_relaxed);
+  return v;
+}
+
 Plan make_plan(int tile_m, int M, int N, int K, int sm_count, size_t budget,
-               bool allow_stream_k) {
+               bool allow_stream_k, int pairs) {
+  // Work units are tiles of tile_m rows x (128 * cg) columns, one per CTA or
+  // CTA pair; `units` of them run at once (pairs: `pairs` when given, else
+  // sm_count / 2).
+  const int cg = choose_cg(tile_m, N, sm_count);
+  const int units = cg == 2 ? (pairs > 0 ? pairs : sm_count / 2) : sm_count;
   Plan p;
-  const int tiles = ((M + tile_m - 1) / tile_m) * (N / TILE_N);
+  p.cg = cg;
+  const int tiles = ((M + tile_m - 1) / tile_m) * (N / (TILE_N * cg));
   const int kblocks = K / BK;
   const int promo = promote_blocks();
   p.sched = Sched{tiles, 1, tiles, 0, 0, promo};
-  p.grid = tiles < sm_count ? tiles : sm_count;
+  p.grid = cg * (tiles < units ? tiles : units);
   p.workspace_bytes = 0;
   if (budget == 0) return p;
-  const int waves = tiles / sm_count;
-  const int rem = tiles - waves * sm_count;
-  if (rem == 0 || rem * 4 > static_cast<int>(kTicketBytes)) return p;
-  const size_t tile_bytes = static_cast<size_t>(tile_m) * TILE_N * 4;
+  const int waves = tiles / units;
+  const int rem = tiles - waves * units;
+  if (rem == 0 || rem * cg * 4 > static_cast<int>(kTicketBytes)) return p;
+  const size_t tile_bytes = static_cast<size_t>(cg) * tile_m * TILE_N * 4;
   const double t_tile = kblocks * (tile_m > 128 ? kBlockUs256 : kBlockUs128);
   double best = (waves + 1) * t_tile;  // whole tiles
 
   // equal splits of each tail tile: at most four, each at least eight blocks
-  int f = sm_count / rem;
+  int f = units / rem;
   f = f < 4 ? f : 4;
   f = f < kblocks / 8 ? f : kblocks / 8;
   const size_t split_bytes = kTicketBytes + static_cast<size_t>(rem) * f * tile_bytes;
   if (f >= 2 && split_bytes <= budget && (waves + 1.0 / f) * t_tile + kSplitUs < best) {
     best = (waves + 1.0 / f) * t_tile + kSplitUs;
-    p.sched = Sched{waves * sm_count, f, waves * sm_count + rem * f, 0, 0, promo};
-    p.grid = p.sched.items < sm_count ? p.sched.items : sm_count;
+    p.sched = Sched{waves * units, f, waves * units + rem * f, 0, 0, promo};
+    p.grid = cg * (p.sched.items < units ? p.sched.items : units);
     p.workspace_bytes = split_bytes;
   }
   if (allow_stream_k) {
-    // equal shares of the tail's blocks, one per CTA: at least eight blocks
+    // equal shares of the tail's blocks, one per unit: at least eight blocks
     // each, at most four shares per tile, more shares than tiles
     const long run = static_cast<long>(rem) * kblocks;
-    int chunks = sm_count;
+    int chunks = units;
     chunks = chunks < 3 * rem ? chunks : 3 * rem;
     chunks = static_cast<long>(chunks) < run / 8 ? chunks : static_cast<int>(run / 8);
     int most = 0;
@@ -889,69 +1014,78 @@ Plan make_plan(int tile_m, int M, int N, int K, int sm_count, size_t budget,
     const double sk_time = (waves + static_cast<double>(rem) / chunks) * t_tile + kStreamKUs;
     if (chunks > rem && most <= 4 && run * chunks < (1l << 31) && sk_bytes <= budget &&
         sk_time < best) {
-      p.sched = Sched{waves * sm_count, 1, 0, chunks, rem, promo};
-      p.grid = waves > 0 ? sm_count : chunks;
+      p.sched = Sched{waves * units, 1, 0, chunks, rem, promo};
+      p.grid = cg * (waves > 0 ? units : chunks);
       p.workspace_bytes = sk_bytes;
     }
   }
   return p;
 }
 
-template <int TILE_M, int GROUP, int OUT>
+template <int TILE_M, int GROUP, int OUT, int CG>
 cudaError_t launch_impl(const CUtensorMap& act_map, const uint8_t* tiles, const __half* scales,
                         const Outputs& out, int M, int N, int K, const Plan& plan, void* workspace,
                         int* status, unsigned long long wait_limit_ns, cudaStream_t stream) {
-  using L = Cfg<TILE_M>;
-  auto kernel = gemm_tc_kernel<TILE_M, GROUP, OUT>;
+  using L = Cfg<TILE_M, CG>;
+  auto kernel = gemm_tc_kernel<TILE_M, GROUP, OUT, CG>;
   static std::atomic<uint64_t> configured{0};  // devices set, per instantiation
   cudaError_t e = ensure_dynamic_smem(kernel, L::DYN_BYTES, configured);
   if (e != cudaSuccess) return e;
-  const int grid = plan.grid;
   uint32_t* tickets = static_cast<uint32_t*>(workspace);
   float* partials = workspace ? reinterpret_cast<float*>(static_cast<char*>(workspace) +
                                                          kTicketBytes)
                               : nullptr;
-  kernel<<<grid, THREADS, L::DYN_BYTES, stream>>>(act_map, tiles, scales, out, M, N, K,
-                                                  plan.sched, tickets, partials, status,
-                                                  wait_limit_ns);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(plan.grid);
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = L::DYN_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CG;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = CG > 1 ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, act_map, tiles, scales, out, M, N, K, plan.sched,
+                            tickets, partials, status, wait_limit_ns);
 }
 
-template <int TILE_M, int OUT>
+template <int TILE_M, int OUT, int CG>
 cudaError_t launch_group(const CUtensorMap& act_map, const uint8_t* tiles,
                          const __half* scales, const Outputs& out, int M, int N, int K,
                          int group, const Plan& plan, void* workspace, int* status,
                          unsigned long long wait_limit_ns, cudaStream_t stream) {
   switch (group) {
     case 32:
-      return launch_impl<TILE_M, 32, OUT>(act_map, tiles, scales, out, M, N, K, plan,
-                                               workspace, status, wait_limit_ns, stream);
+      return launch_impl<TILE_M, 32, OUT, CG>(act_map, tiles, scales, out, M, N, K, plan,
+                                              workspace, status, wait_limit_ns, stream);
     case 64:
-      return launch_impl<TILE_M, 64, OUT>(act_map, tiles, scales, out, M, N, K, plan,
-                                               workspace, status, wait_limit_ns, stream);
+      return launch_impl<TILE_M, 64, OUT, CG>(act_map, tiles, scales, out, M, N, K, plan,
+                                              workspace, status, wait_limit_ns, stream);
     default:
-      return launch_impl<TILE_M, 128, OUT>(act_map, tiles, scales, out, M, N, K, plan,
+      return launch_impl<TILE_M, 128, OUT, CG>(act_map, tiles, scales, out, M, N, K, plan,
                                                workspace, status, wait_limit_ns, stream);
   }
 }
 
 template <int TILE_M, int GROUP>
 KernelConfig config_of() {
-  using L = Cfg<TILE_M>;
+  using L = Cfg<TILE_M, 1>;
   return KernelConfig{TILE_M, TILE_N, BK, TILE_N, TILE_M, L::A_STAGES, THREADS, L::DYN_BYTES};
 }
 
 template <int TILE_M, int GROUP>
 cudaError_t resources_of(KernelResources* out) {
-  auto kernel = gemm_tc_kernel<TILE_M, GROUP, kOutHalf>;
+  auto kernel = gemm_tc_kernel<TILE_M, GROUP, kOutHalf, 1>;
   static std::atomic<uint64_t> configured{0};
-  cudaError_t e = ensure_dynamic_smem(kernel, Cfg<TILE_M>::DYN_BYTES, configured);
+  cudaError_t e = ensure_dynamic_smem(kernel, Cfg<TILE_M, 1>::DYN_BYTES, configured);
   if (e != cudaSuccess) return e;
   cudaFuncAttributes a{};
   if ((e = cudaFuncGetAttributes(&a, kernel)) != cudaSuccess) return e;
   int active = 0;
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&active, kernel, THREADS,
-                                                    Cfg<TILE_M>::DYN_BYTES);
+                                                    Cfg<TILE_M, 1>::DYN_BYTES);
   if (e != cudaSuccess) return e;
   *out = KernelResources{a.numRegs, static_cast<int>(a.sharedSizeBytes), a.maxThreadsPerBlock,
                          active};
@@ -991,16 +1125,19 @@ cudaError_t launch(const CUtensorMap& act_map, int tile_m, const uint8_t* tiles,
   const bool plain = out.count == 1 && out.ldc == N && out.col0 == 0;
   if (fp32_out && !plain) return cudaErrorInvalidValue;  // float C is one plain matrix
   const int kind = fp32_out ? kOutFloat : (plain ? kOutHalf : kOutHalfCopies);
-#define I4G_TC_CASE(TM, KIND)                                                              \
-  if (tile_m == TM && kind == KIND)                                                        \
-    return launch_group<TM, KIND>(act_map, tiles, scales, out, M, N, K, group, plan,       \
-                                  workspace, status, wait_limit_ns, stream);
-  I4G_TC_CASE(128, kOutHalf)
-  I4G_TC_CASE(128, kOutFloat)
-  I4G_TC_CASE(128, kOutHalfCopies)
-  I4G_TC_CASE(256, kOutHalf)
-  I4G_TC_CASE(256, kOutFloat)
-  I4G_TC_CASE(256, kOutHalfCopies)
+#define I4G_TC_CASE(TM, KIND, CG)                                                          \
+  if (tile_m == TM && kind == KIND && plan.cg == CG)                                       \
+    return launch_group<TM, KIND, CG>(act_map, tiles, scales, out, M, N, K, group, plan,   \
+                                      workspace, status, wait_limit_ns, stream);
+  I4G_TC_CASE(128, kOutHalf, 1)
+  I4G_TC_CASE(128, kOutFloat, 1)
+  I4G_TC_CASE(128, kOutHalfCopies, 1)
+  I4G_TC_CASE(256, kOutHalf, 1)
+  I4G_TC_CASE(256, kOutFloat, 1)
+  I4G_TC_CASE(256, kOutHalfCopies, 1)
+  I4G_TC_CASE(256, kOutHalf, 2)
+  I4G_TC_CASE(256, kOutFloat, 2)
+  I4G_TC_CASE(256, kOutHalfCopies, 2)
 #undef I4G_TC_CASE
   return cudaErrorInvalidValue;
 }

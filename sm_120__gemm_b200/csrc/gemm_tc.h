@@ -70,13 +70,19 @@ int promote_blocks();
 
 struct Plan {
   Sched sched;
-  int grid;
+  int grid;                // CTAs
+  int cg;                  // CTAs per tile: 1, or 2 (a CTA pair, cluster of two)
   size_t workspace_bytes;  // 0 when nothing is split
 };
+// CTAs per tile the plan for these sizes uses (activation rows per CTA: tile_m / cg).
+int choose_cg(int tile_m, int N, int sm_count);
 // The schedule for a workspace of `budget` bytes (0: none): stream-K when it
 // fits (and allow_stream_k), else equal splits when they fit, else whole tiles.
+// pairs: CTA pairs resident at once on the device (max_pairs; 0: sm_count / 2).
 Plan make_plan(int tile_m, int M, int N, int K, int sm_count, size_t budget,
-               bool allow_stream_k);
+               bool allow_stream_k, int pairs = 0);
+// CTA pairs of the paired kernel that fit on the current device at once.
+int max_pairs(int sm_count);
 
 // TILE_M (activation rows per tile, the MMA-N) for a problem on sm_count SMs.
 int choose_tile_m(int M, int N, int sm_count);

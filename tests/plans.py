@@ -17,25 +17,41 @@ def sm_count():
     return torch.cuda.get_device_properties(0).multi_processor_count
 
 
-def expected_plan(M, N, K, budget=1 << 62, sms=None):
+def device_pairs():
+    import sm_120__gemm_b200 as m
+    return m.max_pairs()
+
+
+def plan_cg(tile_m, N):
+    """CTAs per tile: 2 (a CTA pair) for 256-row tiles of N % 256 == 0."""
+    return 2 if tile_m == 256 and N % 256 == 0 else 1
+
+
+def expected_plan(M, N, K, budget=1 << 62, sms=None, pairs=None):
     """The tcgen05 schedule for this shape: (kind, workspace bytes, tile_m)
-    with kind "stream-k", "split<F>" or "whole"."""
-    sms = sms or sm_count()
+    with kind "stream-k", "split<F>" or "whole". Work units are tiles of
+    tile_m rows x 128 * cg columns; `pairs` resident CTA pairs (default: the
+    current device's when sms is not given, else sms // 2)."""
+    if sms is None:
+        sms = sm_count()
+        pairs = pairs or device_pairs()
     tile_m = 128 if M <= 128 else 256
-    tiles = -(-M // tile_m) * (N // TILE_N)
+    cg = plan_cg(tile_m, N)
+    units = (pairs or sms // 2) if cg == 2 else sms
+    tiles = -(-M // tile_m) * (N // (TILE_N * cg))
     kb = K // 64
-    waves, rem = divmod(tiles, sms)
-    tile_bytes = tile_m * TILE_N * 4
-    if rem == 0 or rem * 4 > TICKET_BYTES:
+    waves, rem = divmod(tiles, units)
+    tile_bytes = cg * tile_m * TILE_N * 4
+    if rem == 0 or rem * cg * 4 > TICKET_BYTES:
         return "whole", 0, tile_m
     t_tile = kb * (0.45 if tile_m > 128 else 0.5)
     best, plan = (waves + 1) * t_tile, ("whole", 0, tile_m)
-    f = min(4, sms // rem, kb // 8)
+    f = min(4, units // rem, kb // 8)
     need = TICKET_BYTES + rem * f * tile_bytes
     if f >= 2 and need <= budget and (waves + 1.0 / f) * t_tile + 12.0 < best:
         best, plan = (waves + 1.0 / f) * t_tile + 12.0, (f"split{f}", need, tile_m)
     run = rem * kb
-    chunks = min(sms, 3 * rem, run // 8)
+    chunks = min(units, 3 * rem, run // 8)
     if chunks > rem:
         most = max((((t + 1) * kb) * chunks - 1) // run - ((t * kb + 1) * chunks - 1) // run + 1
                    for t in range(rem))

@@ -132,7 +132,7 @@ def test_kernel_config_needs_no_gpu():
     import sm_120__gemm_b200 as m
     c = m.kernel_config(m.VARIANT_TC, 256, 128)
     assert (c["rows"], c["cols"], c["bk"], c["mma_m"], c["mma_n"]) == (256, 128, 64, 128, 256)
-    assert c["threads"] == 864 and 0 < c["dynamic_smem_bytes"] <= 232448
+    assert c["threads"] == 736 and 0 < c["dynamic_smem_bytes"] <= 232448
     d = m.kernel_config(m.VARIANT_DECODE, 16, 64)
     assert d["rows"] == 16 and d["cols"] == 128 and d["stages"] >= 2
     with pytest.raises(m.I4GError):

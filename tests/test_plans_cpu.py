@@ -5,7 +5,8 @@ workspace sizes. The GPU tests rely on the same mirrors to know which
 schedule a shape runs."""
 import pytest
 
-from plans import TICKET_BYTES, TILE_N, decode_cluster, expected_decode_plan, expected_plan
+from plans import (TICKET_BYTES, TILE_N, decode_cluster, expected_decode_plan, expected_plan,
+                   plan_cg)
 
 MS = (1, 5, 8, 9, 16, 17, 100, 128, 129, 300, 512, 1000, 1024, 4096, 8192)
 NS = (128, 640, 1024, 4096, 7168, 14336, 28672)
@@ -38,15 +39,16 @@ def test_plan_query_matches_the_mirrors(i4g, sms):
                     else:
                         kind, need, tile_m = expected_plan(M, N, K, budget=budget, sms=sms)
                         kern = f"tcgen05/{tile_m}"
+                        cg = plan_cg(tile_m, N)
+                        units = sms // cg
+                        tiles = -(-M // tile_m) * (N // (TILE_N * cg))
                         if kind == "whole":
-                            tiles = -(-M // tile_m) * (N // TILE_N)
-                            want = (kern, "whole", min(tiles, sms), 0)
+                            want = (kern, "whole", cg * min(tiles, units), 0)
                         elif kind.startswith("split"):
                             want = (kern, "split", int(kind[5:]), need)
                         else:
-                            tiles = -(-M // tile_m) * (N // TILE_N)
-                            rem = tiles % sms
-                            chunks = (need - TICKET_BYTES) // (tile_m * TILE_N * 4) - rem + 1
+                            rem = tiles % units
+                            chunks = (need - TICKET_BYTES) // (cg * tile_m * TILE_N * 4) - rem + 1
                             want = (kern, "stream-k", chunks, need)
                     have = (got["kernel"], got["schedule"], got["param"], got["workspace_bytes"])
                     assert have == want, (M, N, K, budget, sms, have, want)
