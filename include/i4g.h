@@ -244,8 +244,8 @@ int i4g_shard_range(int K, int N, int group, int world, int rank,
  *              activation tiles) or I4G_PLAN_KERNEL_DECODE
  *   *schedule: tcgen05: WHOLE (*param = grid), SPLIT (*param = ways each
  *              tail tile is split), STREAMK (*param = tail shares);
- *              decode: CLUSTER (*param = cluster size), STREAMK (*param =
- *              grid)
+ *              decode: SLICES (*param = grid), CLUSTER (*param = cluster
+ *              size), STREAMK (*param = grid)
  *   *bytes:    workspace bytes that schedule uses
  * fp32_out: as i4g_gemm_fp32 (never the decode kernel). */
 enum {
@@ -257,7 +257,8 @@ enum {
   I4G_PLAN_WHOLE = 0,
   I4G_PLAN_SPLIT = 1,
   I4G_PLAN_STREAMK = 2,
-  I4G_PLAN_CLUSTER = 3
+  I4G_PLAN_CLUSTER = 3,
+  I4G_PLAN_SLICES = 4
 };
 int i4g_plan(int M, int N, int K, int group, int fp32_out, int sm_count,
              size_t workspace_bytes, int* kernel, int* schedule, int* param,
@@ -303,19 +304,24 @@ int i4g_kernel_resources(int variant, int rows, int group, i4g_kernel_resources_
 
 /* ---- decode schedule (no counterpart in the reference) --------------------- */
 
-/* The decode kernel (M <= 16, FP16 C) has two schedules: the cluster schedule
+/* The decode kernel (M <= 16, FP16 C) has three schedules: the slice schedule
+ * (each CTA owns a run of 16-column slices over all of K; needs no
+ * workspace; possible when N / 16 <= 8 x the SM count), the cluster schedule
  * (each 128-column tile's K split over a thread-block cluster, reduced
  * through distributed shared memory; needs no workspace) and the stream-K
  * schedule of the *_ws entry points (see the workspace section). AUTO (the
- * default, or the I4G_DECODE_SCHEDULE environment variable's "cluster" /
- * "streamk" at the first call) picks stream-K when it takes enough work off
- * the busiest SM to pay for its reduction through global memory; the others
- * force one (stream-K only where a large enough workspace is given).
+ * default, or the I4G_DECODE_SCHEDULE environment variable's "slices" /
+ * "cluster" / "streamk" at the first call) takes the slice schedule where it
+ * is possible, else stream-K when it takes enough work off the busiest SM to
+ * pay for its reduction through global memory, else the cluster schedule;
+ * the others force one (slices where possible, stream-K only where a large
+ * enough workspace is given, the cluster schedule otherwise).
  * Process-wide; affects launches issued after the call. */
 enum {
   I4G_DECODE_AUTO = 0,
   I4G_DECODE_CLUSTER = 1,
-  I4G_DECODE_STREAMK = 2
+  I4G_DECODE_STREAMK = 2,
+  I4G_DECODE_SLICES = 3
 };
 int i4g_set_decode_schedule(int schedule);
 

@@ -341,7 +341,7 @@ def peer_barrier(local_flags: int, peer_flags, world: int, rank: int, epoch: int
 
 
 PLAN_KERNELS = {0: "tcgen05/256", 1: "tcgen05/128", 2: "decode"}
-PLAN_SCHEDULES = {0: "whole", 1: "split", 2: "stream-k", 3: "cluster"}
+PLAN_SCHEDULES = {0: "whole", 1: "split", 2: "stream-k", 3: "cluster", 4: "slices"}
 
 
 def plan(M: int, N: int, K: int, group: int, sm_count: int, workspace_bytes: int = 0,
@@ -382,11 +382,11 @@ def max_pairs() -> int:
     return v.value
 
 
-DECODE_SCHEDULES = {"auto": 0, "cluster": 1, "streamk": 2}
+DECODE_SCHEDULES = {"auto": 0, "cluster": 1, "streamk": 2, "slices": 3}
 
 
 def set_decode_schedule(schedule: str) -> None:
-    """C ABI i4g_set_decode_schedule: "auto", "cluster" or "streamk", for
+    """C ABI i4g_set_decode_schedule: "auto", "slices", "cluster" or "streamk", for
     decode-shaped (M <= 16) launches issued after the call, process-wide."""
     _call("i4g_set_decode_schedule", DECODE_SCHEDULES[schedule])
 

@@ -192,6 +192,64 @@ int act_map(const void* A, int M, int K, int rows, const CUtensorMap** out) {
   return I4G_OK;
 }
 
+// The decode slice schedule's weight tensor maps over one weight buffer
+// ({256 bytes, 8 slices, 2 halves, K/64 blocks, N/128 tiles}, strides 256,
+// 2048, 4096 and (K/64) * 4096 bytes; map n-1 has a box of n slices x 2
+// halves x 4 blocks). Cached per host thread like the activation maps.
+struct SliceMapEntry {
+  int device = -1;
+  const void* tiles = nullptr;
+  int N = 0, K = 0;
+  unsigned long long used = 0;
+  i4g::dec::SliceMaps maps;
+};
+
+int slice_maps(const void* tiles, int N, int K, const i4g::dec::SliceMaps** out) {
+  constexpr int kEntries = 4;
+  thread_local SliceMapEntry cache[kEntries];
+  thread_local unsigned long long clock = 0;
+  int dev = -1;
+  cudaGetDevice(&dev);
+  ++clock;
+  SliceMapEntry* victim = &cache[0];
+  for (SliceMapEntry& e : cache) {
+    if (e.device == dev && e.tiles == tiles && e.N == N && e.K == K) {
+      e.used = clock;
+      *out = &e.maps;
+      return I4G_OK;
+    }
+    if (e.used < victim->used) victim = &e;
+  }
+  EncodeTiledFn encode = nullptr;
+  int st = encode_fn(&encode);
+  if (st != I4G_OK) return st;
+  const cuuint64_t dims[5] = {256, 8, 2, static_cast<cuuint64_t>(K / 64),
+                              static_cast<cuuint64_t>(N / 128)};
+  const cuuint64_t strides[4] = {256, 2048, 4096, static_cast<cuuint64_t>(K / 64) * 4096};
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  for (int n = 1; n <= i4g::dec::kSliceMax; ++n) {
+    const cuuint32_t box[5] = {256, static_cast<cuuint32_t>(n), 2, 4, 1};
+    const CUresult r = encode(&victim->maps.box[n - 1], CU_TENSOR_MAP_DATA_TYPE_UINT8, 5,
+                              const_cast<void*>(tiles), dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      victim->device = -1;
+      victim->used = 0;
+      return fail(I4G_ERR_DRIVER, "cuTensorMapEncodeTiled (weight slices) failed with CUresult %d",
+                  int(r));
+    }
+  }
+  victim->device = dev;
+  victim->tiles = tiles;
+  victim->N = N;
+  victim->K = K;
+  victim->used = clock;
+  *out = &victim->maps;
+  return I4G_OK;
+}
+
 unsigned long long g_wait_limit_ns = kDefaultWaitLimitNs;
 
 using MemRangeFn = int (*)(unsigned long long*, size_t*, unsigned long long);
@@ -283,7 +341,13 @@ int gemm_common(const void* A, const uint8_t* tiles, const void* scales, const i
     const CUtensorMap* dmap = nullptr;
     st = act_map(A, M, K, -i4g::dec::rows_for(M), &dmap);
     if (st != I4G_OK) return st;
-    return finish(i4g::dec::launch(*dmap, tiles, sc, out, M, N, K, group, dev->sm_count,
+    const i4g::dec::SliceMaps* smaps = nullptr;
+    if (i4g::dec::pick_schedule(M, N, K, dev->sm_count, workspace ? workspace_bytes : 0) ==
+        i4g::dec::kScheduleSlices) {
+      st = slice_maps(tiles, N, K, &smaps);
+      if (st != I4G_OK) return st;
+    }
+    return finish(i4g::dec::launch(*dmap, smaps, tiles, sc, out, M, N, K, group, dev->sm_count,
                                    workspace, workspace ? workspace_bytes : 0,
                                    dev->status_word, g_wait_limit_ns, s),
                   "decode kernel launch");
@@ -555,9 +619,10 @@ int i4g_gemm_workspace_size(int M, int N, int K, size_t* bytes) {
   *bytes = i4g::tc::make_plan(tc_tile_m(M, N, dev), M, N, K, dev->sm_count, SIZE_MAX, true,
                               i4g::tc::max_pairs(dev->sm_count))
                .workspace_bytes;
-  if (i4g::dec::supported(M, K, 32)) {  // FP16 C at these M runs the decode kernel
+  if (i4g::dec::supported(M, K, 32) &&  // FP16 C at these M runs the decode kernel
+      i4g::dec::pick_schedule(M, N, K, dev->sm_count, SIZE_MAX) == i4g::dec::kScheduleStreamK) {
     const i4g::dec::SkPlan sk = i4g::dec::sk_plan(M, N, K, dev->sm_count);
-    if (sk.preferred && sk.workspace_bytes > *bytes) *bytes = sk.workspace_bytes;
+    if (sk.workspace_bytes > *bytes) *bytes = sk.workspace_bytes;
   }
   return I4G_OK;
 }
@@ -587,11 +652,12 @@ int i4g_gemm_static_scratch(const void* A, const uint8_t* tiles, const void* sca
                               i4g::tc::max_pairs(dev->sm_count))
                .workspace_bytes;
   } else {
-    // the decode kernel's stream-K schedule when its workspace fits the
-    // static scratch; otherwise its cluster schedule, which needs none
-    const i4g::dec::SkPlan sk = i4g::dec::sk_plan(M, N, K, dev->sm_count);
-    if (sk.preferred && sk.workspace_bytes <= i4g::static_scratch_bytes())
-      need = sk.workspace_bytes;
+    // the decode kernel's stream-K schedule when it is the one chosen and its
+    // workspace fits the static scratch; the slice and cluster schedules
+    // need none
+    if (i4g::dec::pick_schedule(M, N, K, dev->sm_count, i4g::static_scratch_bytes()) ==
+        i4g::dec::kScheduleStreamK)
+      need = i4g::dec::sk_plan(M, N, K, dev->sm_count).workspace_bytes;
   }
   if (need > i4g::static_scratch_bytes()) {
     std::snprintf(t_last_error, sizeof(t_last_error),
@@ -716,7 +782,12 @@ int i4g_plan(int M, int N, int K, int group, int fp32_out, int sm_count,
   if (!fp32_out && i4g::dec::supported(M, K, group)) {
     *kernel = I4G_PLAN_KERNEL_DECODE;
     const i4g::dec::SkPlan sk = i4g::dec::sk_plan(M, N, K, sm_count);
-    if (workspace_bytes > 0 && sk.preferred && workspace_bytes >= sk.workspace_bytes) {
+    const int sched = i4g::dec::pick_schedule(M, N, K, sm_count, workspace_bytes);
+    if (sched == i4g::dec::kScheduleSlices) {
+      *schedule = I4G_PLAN_SLICES;
+      *param = i4g::dec::slice_grid(N, sm_count);
+      *bytes = 0;
+    } else if (sched == i4g::dec::kScheduleStreamK) {
       *schedule = I4G_PLAN_STREAMK;
       *param = sk.grid;
       *bytes = sk.workspace_bytes;
@@ -791,11 +862,12 @@ int i4g_max_pairs(int* pairs) {
 
 int i4g_set_decode_schedule(int schedule) {
   if (schedule != I4G_DECODE_AUTO && schedule != I4G_DECODE_CLUSTER &&
-      schedule != I4G_DECODE_STREAMK)
+      schedule != I4G_DECODE_STREAMK && schedule != I4G_DECODE_SLICES)
     return fail(I4G_ERR_VARIANT, "unknown decode schedule %d", schedule);
   static_assert(I4G_DECODE_AUTO == i4g::dec::kScheduleAuto &&
                     I4G_DECODE_CLUSTER == i4g::dec::kScheduleCluster &&
-                    I4G_DECODE_STREAMK == i4g::dec::kScheduleStreamK,
+                    I4G_DECODE_STREAMK == i4g::dec::kScheduleStreamK &&
+                    I4G_DECODE_SLICES == i4g::dec::kScheduleSlices,
                 "decode schedule codes");
   i4g::dec::set_schedule(schedule);
   return I4G_OK;

@@ -685,6 +685,261 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM)
   if (out.count > 1) __threadfence_system();  // peer copies are read by other GPUs
 }
 
+// ---------------------------------------------------------------------------
+// Slice schedule. The columns are cut into 16-column slices (one mma.sync
+// A operand each) and CTA c (one per SM) owns the contiguous run of slices
+// [c*S/G, (c+1)*S/G) over all of K, so no two CTAs share an output and
+// nothing is reduced across CTAs, and every SM streams the same number of
+// weight bytes to within one slice. A run spans at most two 128-column tiles
+// of the layout; per ring stage (four 64-k blocks) one thread fetches each
+// tile segment's slices with one 5-D TMA box ({256 bytes of a slice-half,
+// slices, 2 halves, 4 blocks}), its scale groups with one bulk copy, and
+// the activation rows with the 3-D box of the other schedules. Sixteen
+// warps take the stage's (slice, block) units round robin, unit u =
+// slice * 4 + block going to warp u % 16, so the four SMSPs get equal
+// shares; each warp keeps the sums of its (slice, block-of-stage) units over
+// all stages, and at the end the four block-parts of each slice are added in
+// order through shared memory (deterministic).
+
+constexpr int SLICE_COLS = 16;
+constexpr int SL_WARPS = 16;                      // all of them compute
+constexpr int SL_THREADS = SL_WARPS * 32;
+constexpr int SL_MAX = 8;                         // slices a CTA may own
+constexpr int SL_UNITS = SL_MAX * KPS;            // (slice, block) units per stage, at most
+
+using SliceMaps = ::i4g::dec::SliceMaps;
+static_assert(SL_MAX == kSliceMax, "slice bound");
+
+template <int MT, int GROUP, int STAGES>
+struct SliceLayout {
+  static constexpr int ROWS = MT * 8;
+  static constexpr int ABYTES = KPS * ROWS * BK * 2;      // activation box, swizzled
+  static constexpr int WBYTES = SL_MAX * KPS * 2 * 256;   // up to eight slices
+  static constexpr int SGROUPS = KPS * BK / GROUP + (GROUP > BK ? 1 : 0);
+  static constexpr int SBYTES = 2 * SGROUPS * 256;        // up to two tile segments
+  static constexpr int SLOT = ((ABYTES + WBYTES + SBYTES + 1023) / 1024) * 1024;
+  static constexpr int BARS = STAGES * SLOT;              // full[], empty[]
+  static constexpr int ABORT = BARS + 2 * STAGES * 8;
+  static constexpr int DYN = ABORT + 16 + 1024;
+  // the final cross-warp sums reuse the ring: [unit][lane][MT * 4] floats
+  static_assert(SL_UNITS * 32 * MT * 4 * 4 <= BARS, "reduction scratch fits the ring");
+};
+
+template <int MT, int GROUP>
+constexpr int slice_stages() {
+  int s = 8;
+  while (s > 2 && SliceLayout<MT, GROUP, 8>::SLOT * s + 2 * s * 8 + 16 + 1024 + 1024 >
+                      SMEM_PER_SM)
+    --s;
+  return s;
+}
+
+// Writes one lane's four sums of the fragment of slice column base `col`
+// (16 columns) and row block mb to every copy of C (as store_fragment).
+__device__ __forceinline__ void store_slice_fragment(const Outputs& out, int M, int col, int ln,
+                                                     int mb, float4 v) {
+  const int c = col + (ln >> 2);
+  const int m = mb * 8 + 2 * (ln & 3);
+  const size_t ldc = static_cast<size_t>(out.ldc);
+  const size_t off = static_cast<size_t>(m) * ldc + out.col0 + c;
+  const __half hx = __float2half_rn(v.x), hy = __float2half_rn(v.y);
+  const __half hz = __float2half_rn(v.z), hw = __float2half_rn(v.w);
+#pragma unroll 1
+  for (int d = 0; d < out.count; ++d) {
+    __half* c0 = static_cast<__half*>(out.dst[d]) + off;
+    if (m < M) {
+      c0[0] = hx;
+      c0[8] = hz;
+    }
+    if (m + 1 < M) {
+      c0[ldc] = hy;
+      c0[ldc + 8] = hw;
+    }
+  }
+}
+
+template <int MT, int GROUP, int STAGES>
+__global__ void __launch_bounds__(SL_THREADS, 1)
+    decode_slices_kernel(const __grid_constant__ CUtensorMap act_map,
+                         const __grid_constant__ SliceMaps wmaps,
+                         const __half* __restrict__ scales, const __grid_constant__ Outputs out,
+                         int M, int N, int K, int* status, unsigned long long wait_limit_ns) {
+  using L = SliceLayout<MT, GROUP, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const uint32_t ring = smem_u32(smem);
+  const uint32_t bars = ring + L::BARS;  // full[STAGES], empty[STAGES]
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::ABORT);
+  volatile int* never = abort_flag + 2;  // a flag nobody sets (draining waits)
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int kblocks = K / BK;
+  const int groups = K / GROUP;
+  const int nslices = N / SLICE_COLS;
+  const int s0 = static_cast<int>((static_cast<long>(blockIdx.x) * nslices) / gridDim.x);
+  const int s1 = static_cast<int>((static_cast<long>(blockIdx.x + 1) * nslices) / gridDim.x);
+  const int nsl = s1 - s0;                         // 1 .. SL_MAX (host-checked)
+  const int tile0 = s0 / 8;
+  const int n0 = min(nsl, 8 - s0 % 8);             // slices in the first tile segment
+  const int n1 = nsl - n0;                         // in the next tile
+  const int nstages = (kblocks + KPS - 1) / KPS;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(bars + 8 * s, 1);
+      mbar_init(bars + 8 * (STAGES + s), SL_WARPS);
+    }
+    *abort_flag = 0;
+    *never = 0;
+    fence_mbarrier_init();
+    fence_proxy_async_smem();
+  }
+  __syncthreads();
+
+  // Ring feeder: lane 0 of warp 0, which also computes (a separate producer
+  // warp would leave the 16-row instance too few registers). It issues
+  // stages 0 .. STAGES-1 up front and then, after its own part of stage i,
+  // refills the slot stage i-1 used (for stage i-1+STAGES) once every warp
+  // has released it; one stage of slack keeps it from waiting on the
+  // slowest warp's current stage.
+  const bool feeder = threadIdx.x == 0;
+  int issued = 0;   // stages issued so far (the feeder's count)
+  bool fed = true;  // false once the feeder gave up on a wait
+  auto issue = [&](int i) {
+    const int s = i % STAGES;
+    const int kb = i * KPS;
+    const int nkb = min(KPS, kblocks - kb);
+    const int g0 = kb * BK / GROUP;
+    const int g1 = ((kb + nkb) * BK + GROUP - 1) / GROUP;
+    const uint32_t slot = ring + s * L::SLOT;
+    const uint32_t full = bars + 8 * s;
+    // full boxes count even where they reach past K (zero fill)
+    mbar_arrive_expect_tx(full, L::ABYTES + nsl * KPS * 2 * 256 +
+                                    (n1 > 0 ? 2 : 1) * (g1 - g0) * 256);
+    tma_load_3d(slot, &act_map, full, 0, 0, kb);
+    const uint32_t w0 = slot + L::ABYTES;
+    tma_load_5d(w0, &wmaps.box[n0 - 1], full, 0, s0 % 8, 0, kb, tile0);
+    const uint32_t sdst = slot + L::ABYTES + L::WBYTES;
+    bulk_load(sdst, scales + (static_cast<size_t>(tile0) * groups + g0) * 128, (g1 - g0) * 256,
+              full);
+    if (n1 > 0) {
+      tma_load_5d(w0 + n0 * KPS * 2 * 256, &wmaps.box[n1 - 1], full, 0, 0, 0, kb, tile0 + 1);
+      bulk_load(sdst + L::SGROUPS * 256,
+                scales + (static_cast<size_t>(tile0 + 1) * groups + g0) * 128, (g1 - g0) * 256,
+                full);
+    }
+  };
+  if (feeder) {
+    prefetch_tensormap(&act_map);
+    prefetch_tensormap(&wmaps.box[n0 - 1]);
+    if (n1 > 0) prefetch_tensormap(&wmaps.box[n1 - 1]);
+    for (; issued < STAGES && issued < nstages; ++issued) issue(issued);
+  }
+
+  // this warp's units: u = warp and warp + 16, u = slice * KPS + block
+  const int g = lane >> 2, t = lane & 3;
+  const uint32_t a0 = g * 128 + (((2 * t) ^ g) << 4);
+  const uint32_t a1 = g * 128 + (((2 * t + 1) ^ g) << 4);
+  const int b = warp % KPS;  // the block of the stage both units take
+  uint32_t woff[2], soff[2];
+  bool own[2];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int u = warp + q * SL_WARPS;
+    own[q] = u < nsl * KPS;
+    const int j = own[q] ? u / KPS : 0;
+    const bool second = j >= n0;
+    const int jl = second ? j - n0 : j;
+    const int ns = second ? n1 : n0;
+    // [block][half][slice][16 columns x 16 bytes] per tile segment
+    woff[q] = L::ABYTES + (second ? n0 * KPS * 2 * 256 : 0) + ((b * 2 + (t >> 1)) * ns + jl) * 256 +
+              g * 16 + (t & 1) * 8;
+    soff[q] = L::ABYTES + L::WBYTES + (second ? L::SGROUPS * 256 : 0) +
+              (((s0 + j) % 8) * SLICE_COLS + g) * 2;
+  }
+  const uint32_t aoff = b * (L::ROWS * 128);
+  float acc[2][MT][4][4];
+#pragma unroll
+  for (int q = 0; q < 2; ++q)
+#pragma unroll
+    for (int mb = 0; mb < MT; ++mb)
+#pragma unroll
+      for (int x = 0; x < 4; ++x)
+#pragma unroll
+        for (int y = 0; y < 4; ++y) acc[q][mb][x][y] = 0.0f;
+  for (int i = 0; i < nstages; ++i) {
+    const int s = i % STAGES;
+    const uint32_t ph = (i / STAGES) & 1u;
+    if (!mbar_wait(bars + 8 * s, ph, abort_flag, status, wait_limit_ns)) break;
+    const uint32_t slot = ring + s * L::SLOT;
+    const int kb = i * KPS;
+    if (b < kblocks - kb) {
+      const uint32_t so = scale_offset<GROUP>(b, t, kb & 1);
+#pragma unroll
+      for (int q = 0; q < 2; ++q)
+        if (own[q])
+          block_step(slot + woff[q], slot + soff[q] + so, slot + a0 + aoff, slot + a1 + aoff,
+                     acc[q]);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bars + 8 * (STAGES + s));
+    if (feeder && fed && i >= 1 && issued == i - 1 + STAGES && issued < nstages) {
+      const int r = i - 1;
+      fed = mbar_wait(bars + 8 * (STAGES + r % STAGES), (r / STAGES) & 1u, abort_flag, status,
+                      wait_limit_ns);
+      if (fed) issue(issued++);
+    }
+  }
+  if (feeder && *abort_flag) {
+    // gave up: let the copies already issued land before the ring is reused
+    for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; ++i)
+      mbar_wait(bars + 8 * (i % STAGES), (i / STAGES) & 1u, never, nullptr, 100000000ull);
+  }
+  {
+    // The four block-parts of each slice, added in order through shared
+    // memory: the ring is reused once every warp has passed its last stage
+    // (every copy had landed for it to do so, or was drained above).
+    constexpr int CTHREADS = SL_WARPS * 32;
+    epi_bar_sync(CTHREADS);
+    float4* red = reinterpret_cast<float4*>(smem);  // [unit][lane][MT]
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      if (!own[q]) continue;
+      const int u = warp + q * SL_WARPS;
+#pragma unroll
+      for (int mb = 0; mb < MT; ++mb) {
+        float4 v;
+        v.x = (acc[q][mb][0][0] + acc[q][mb][1][0]) + (acc[q][mb][2][0] + acc[q][mb][3][0]);
+        v.y = (acc[q][mb][0][1] + acc[q][mb][1][1]) + (acc[q][mb][2][1] + acc[q][mb][3][1]);
+        v.z = (acc[q][mb][0][2] + acc[q][mb][1][2]) + (acc[q][mb][2][2] + acc[q][mb][3][2]);
+        v.w = (acc[q][mb][0][3] + acc[q][mb][1][3]) + (acc[q][mb][2][3] + acc[q][mb][3][3]);
+        red[(u * 32 + lane) * MT + mb] = v;
+      }
+    }
+    epi_bar_sync(CTHREADS);
+    // thread -> (slice j, lane ln, row block mb)
+    const int idx = static_cast<int>(threadIdx.x);
+    const int j = idx / (32 * MT);
+    const int ln = (idx / MT) % 32;
+    const int mb = idx % MT;
+    if (j < nsl) {
+      float4 sum = red[((j * KPS) * 32 + ln) * MT + mb];
+#pragma unroll
+      for (int bb = 1; bb < KPS; ++bb) {
+        const float4 v = red[((j * KPS + bb) * 32 + ln) * MT + mb];
+        sum.x += v.x;
+        sum.y += v.y;
+        sum.z += v.z;
+        sum.w += v.w;
+      }
+      store_slice_fragment(out, M, (s0 + j) * SLICE_COLS, ln, mb, sum);
+    }
+    if (out.count > 1) __threadfence_system();  // peer copies are read by other GPUs
+  }
+}
+
 template <int MT, int GROUP>
 cudaError_t launch_typed(const CUtensorMap& act_map, const uint8_t* tiles, const __half* scales,
                          const Outputs& out, int M, int N, int K, int cluster, int* status,
@@ -765,10 +1020,12 @@ int choose_cluster(int N, int K, int sm_count) {
   return best;
 }
 
-// Schedule choice: kScheduleAuto lets the model in sk_plan decide;
-// kScheduleCluster / kScheduleStreamK force one (stream-K only with a large
-// enough workspace). Set by set_schedule; until then, I4G_DECODE_SCHEDULE
-// ("cluster" or "streamk") gives the initial value.
+// Schedule choice: kScheduleAuto takes the slice schedule where slice_grid
+// allows it, else lets the model in sk_plan decide between stream-K and the
+// cluster schedule; kScheduleSlices / kScheduleCluster / kScheduleStreamK
+// force one (slices where possible, stream-K only with a large enough
+// workspace). Set by set_schedule; until then, I4G_DECODE_SCHEDULE
+// ("slices", "cluster" or "streamk") gives the initial value.
 std::atomic<int> g_schedule{-1};
 
 int schedule_mode() {
@@ -778,6 +1035,7 @@ int schedule_mode() {
   int init = kScheduleAuto;
   if (e && std::strcmp(e, "cluster") == 0) init = kScheduleCluster;
   if (e && std::strcmp(e, "streamk") == 0) init = kScheduleStreamK;
+  if (e && std::strcmp(e, "slices") == 0) init = kScheduleSlices;
   int expected = -1;
   g_schedule.compare_exchange_strong(expected, init, std::memory_order_relaxed);
   return g_schedule.load(std::memory_order_relaxed);
@@ -818,6 +1076,29 @@ SkPlan sk_plan(int M, int N, int K, int sm_count) {
   p.preferred = mode == kScheduleStreamK ||
                 (mode == kScheduleAuto && (cluster_work - sk_work) * 13 > 350);
   return p;
+}
+
+template <int MT, int GROUP>
+cudaError_t launch_slices_typed(const CUtensorMap& act_map, const SliceMaps& maps,
+                                const __half* scales, const Outputs& out, int M, int N, int K,
+                                int grid, int* status, unsigned long long wait_limit_ns,
+                                cudaStream_t stream) {
+  constexpr int S = slice_stages<MT, GROUP>();
+  using L = SliceLayout<MT, GROUP, S>;
+  auto kernel = decode_slices_kernel<MT, GROUP, S>;
+  static std::atomic<uint64_t> configured{0};  // devices set, per instantiation
+  cudaError_t e = ensure_dynamic_smem(kernel, L::DYN, configured);
+  if (e != cudaSuccess) return e;
+  kernel<<<grid, SL_THREADS, L::DYN, stream>>>(act_map, maps, scales, out, M, N, K, status,
+                                               wait_limit_ns);
+  return cudaGetLastError();
+}
+
+int slice_grid(int N, int sm_count) {
+  const int slices = N / SLICE_COLS;
+  const int grid = slices < sm_count ? slices : sm_count;
+  if (grid < 1 || (slices + grid - 1) / grid > SL_MAX) return 0;
+  return grid;
 }
 
 template <int MT>
@@ -888,12 +1169,38 @@ bool supported(int M, int K, int group) {
   return M >= 1 && M <= MAX_M;
 }
 
-cudaError_t launch(const CUtensorMap& act_map, const uint8_t* tiles, const __half* scales,
-                   const Outputs& out, int M, int N, int K, int group, int sm_count,
-                   void* workspace, size_t workspace_bytes, int* status,
-                   unsigned long long wait_limit_ns, cudaStream_t stream) {
+int pick_schedule(int M, int N, int K, int sm_count, size_t workspace_bytes) {
+  const int mode = schedule_mode();
+  if ((mode == kScheduleAuto || mode == kScheduleSlices) && slice_grid(N, sm_count) > 0)
+    return kScheduleSlices;
   const SkPlan sk = sk_plan(M, N, K, sm_count);
-  const bool use_sk = workspace && sk.preferred && workspace_bytes >= sk.workspace_bytes;
+  if (workspace_bytes > 0 && sk.preferred && workspace_bytes >= sk.workspace_bytes)
+    return kScheduleStreamK;
+  return kScheduleCluster;
+}
+
+cudaError_t launch(const CUtensorMap& act_map, const SliceMaps* maps, const uint8_t* tiles,
+                   const __half* scales, const Outputs& out, int M, int N, int K, int group,
+                   int sm_count, void* workspace, size_t workspace_bytes, int* status,
+                   unsigned long long wait_limit_ns, cudaStream_t stream) {
+  const int sched = pick_schedule(M, N, K, sm_count, workspace ? workspace_bytes : 0);
+  if (sched == kScheduleSlices) {
+    if (!maps) return cudaErrorInvalidValue;
+    const int grid = slice_grid(N, sm_count);
+#define I4G_SL_CASE(MT, G)                                                                   \
+  if (group == G)                                                                            \
+    return launch_slices_typed<MT, G>(act_map, *maps, scales, out, M, N, K, grid, status,    \
+                                      wait_limit_ns, stream);
+    if (M <= 8) {
+      I4G_SL_CASE(1, 32) I4G_SL_CASE(1, 64) I4G_SL_CASE(1, 128)
+    } else {
+      I4G_SL_CASE(2, 32) I4G_SL_CASE(2, 64) I4G_SL_CASE(2, 128)
+    }
+#undef I4G_SL_CASE
+    return cudaErrorInvalidValue;
+  }
+  const SkPlan sk = sk_plan(M, N, K, sm_count);
+  const bool use_sk = sched == kScheduleStreamK;
   const int cluster = use_sk ? 1 : choose_cluster(N, K, sm_count);
   if (M <= 8)
     return launch_mt<1>(act_map, tiles, scales, out, M, N, K, group, cluster,

@@ -175,6 +175,16 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* map, uint3
       : "memory");
 }
 
+// 5-D tiled TMA load, no multicast.
+__device__ __forceinline__ void tma_load_5d(uint32_t dst, const void* map, uint32_t bar, int c0,
+                                            int c1, int c2, int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(dst),
+      "l"(map), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+      : "memory");
+}
+
 // Contiguous bulk copy global -> shared (16-byte aligned, size % 16 == 0).
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
                                           uint32_t bar) {
@@ -220,8 +230,24 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
   return ok != 0;
 }
 
+// try_wait at cluster scope that may suspend the thread for up to `hint_ns`
+// while the phase is incomplete (as mbar_try_wait_sleep).
+__device__ __forceinline__ bool mbar_try_wait_cluster_sleep(uint32_t bar, uint32_t parity,
+                                                            uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // mbar_wait for a barrier that the other CTA of a pair also arrives on:
-// acquire at cluster scope. Bounded as mbar_wait.
+// acquire at cluster scope. Bounded as mbar_wait; a waiting thread suspends
+// rather than spins.
 __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
                                                   volatile int* abort, int* status,
                                                   uint64_t limit_ns) {
@@ -229,8 +255,8 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
   const uint64_t t0 = global_timer_ns();
   while (true) {
 #pragma unroll 1
-    for (int i = 0; i < 64; ++i)
-      if (mbar_try_wait_cluster(bar, parity)) return true;
+    for (int i = 0; i < 8; ++i)
+      if (mbar_try_wait_cluster_sleep(bar, parity, 20000)) return true;
     if (*abort) return false;
     if (global_timer_ns() - t0 > limit_ns) {
       *abort = 1;

@@ -3,7 +3,8 @@ shape runs and how much workspace it asks for.
 
 expected_plan mirrors the tcgen05 kernel's make_plan and cost model
 (csrc/gemm_tc.cu); expected_decode_plan mirrors the decode kernel's
-choose_cluster and sk_plan (csrc/gemm_decode.cu); expected_workspace is what
+choose_cluster and sk_plan, and expected_decode_schedule its pick_schedule
+and slice_grid (csrc/gemm_decode.cu); expected_workspace is what
 i4g_gemm_workspace_size reports.
 """
 import torch
@@ -11,6 +12,7 @@ import torch
 TICKET_BYTES = 4096  # arrival counters at the start of every workspace
 TILE_N = 128
 DEC_KPS, DEC_BK, DEC_NCOL, DEC_CTAS_PER_SM, DEC_THREADS_C = 4, 64, 128, 2, 256
+DEC_SLICE_COLS, DEC_SLICE_MAX = 16, 8
 
 
 def sm_count():
@@ -95,10 +97,35 @@ def expected_decode_plan(M, N, K, sms=None, schedule="auto"):
     return (cluster_work - sk_work) * 13 > 350, grid, need
 
 
+def decode_slice_grid(N, sms):
+    """CTAs of the slice schedule (one per SM, each owning at most eight
+    16-column slices over all of K); 0 where N is too wide for it."""
+    slices = N // DEC_SLICE_COLS
+    grid = min(slices, sms)
+    if grid < 1 or -(-slices // grid) > DEC_SLICE_MAX:
+        return 0
+    return grid
+
+
+def expected_decode_schedule(M, N, K, budget, sms=None, schedule="auto"):
+    """(schedule, param, workspace bytes) of a decode launch given `budget`
+    bytes of workspace, as i4g_plan reports it: the slice schedule where
+    possible (auto or forced), else stream-K when preferred and the workspace
+    holds it, else the cluster schedule."""
+    sms = sms or sm_count()
+    grid = decode_slice_grid(N, sms)
+    if schedule in ("auto", "slices") and grid:
+        return "slices", grid, 0
+    pref, sk_grid, need = expected_decode_plan(M, N, K, sms=sms, schedule=schedule)
+    if budget > 0 and pref and budget >= need:
+        return "stream-k", sk_grid, need
+    return "cluster", decode_cluster(N, K, sms), 0
+
+
 def expected_workspace(M, N, K, schedule="auto"):
     need = expected_plan(M, N, K)[1]
     if 1 <= M <= 16:
-        pref, _, dec_need = expected_decode_plan(M, N, K, schedule=schedule)
-        if pref:
+        sched, _, dec_need = expected_decode_schedule(M, N, K, 1 << 62, schedule=schedule)
+        if sched == "stream-k":
             need = max(need, dec_need)
     return need

@@ -119,17 +119,18 @@ def test_output_copies_with_stride_and_offset(i4g, M, N, K, grp):
                                    (4, 57344, 8192), (8, 7168, 8192)])
 def test_automatic_schedule_choice(i4g, M, N, K):
     """Under "auto" the workspace query asks for the stream-K bytes exactly
-    when the model prefers stream-K (large N: many column tiles left on one
-    CTA per SM by the cluster schedule); "cluster" never asks for them."""
-    from plans import expected_plan, expected_workspace
+    when the slice schedule is not possible and the model prefers stream-K
+    (large N: many column tiles left on one CTA per SM by the cluster
+    schedule); "slices" and "cluster" never ask for them."""
+    from plans import expected_decode_schedule, expected_plan, expected_workspace
     try:
-        for schedule in ("auto", "cluster", "streamk"):
+        for schedule in ("auto", "slices", "cluster", "streamk"):
             i4g.set_decode_schedule(schedule)
-            pref, _, need = expected_decode_plan(M, N, K, schedule=schedule)
+            sched, _, need = expected_decode_schedule(M, N, K, 1 << 62, schedule=schedule)
             got = i4g.gemm_workspace_size(M, N, K)
-            print(schedule, M, N, K, "stream-k" if pref else "cluster", got)
+            print(schedule, M, N, K, sched, got)
             assert got == expected_workspace(M, N, K, schedule=schedule)
-            assert got == (max(need, expected_plan(M, N, K)[1]) if pref
+            assert got == (max(need, expected_plan(M, N, K)[1]) if sched == "stream-k"
                            else expected_plan(M, N, K)[1])
     finally:
         i4g.set_decode_schedule("streamk")

@@ -78,9 +78,9 @@ def test_argument_checks_need_no_gpu(lib):
     assert lib.i4g_plan(64, 128, 128, 64, 0, 0, 0, *ref) == -2
     assert lib.i4g_plan(64, 128, 128, 64, 0, 148, 0, *ref) == 0
     # decode schedule selector: unknown values are refused, known ones taken
-    assert lib.i4g_set_decode_schedule(3) == -9
+    assert lib.i4g_set_decode_schedule(4) == -9
     assert lib.i4g_set_decode_schedule(-1) == -9
-    for mode in (2, 1, 0):
+    for mode in (3, 2, 1, 0):
         assert lib.i4g_set_decode_schedule(mode) == 0
 
 

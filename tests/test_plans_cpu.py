@@ -5,11 +5,11 @@ workspace sizes. The GPU tests rely on the same mirrors to know which
 schedule a shape runs."""
 import pytest
 
-from plans import (TICKET_BYTES, TILE_N, decode_cluster, expected_decode_plan, expected_plan,
-                   plan_cg)
+from plans import (TICKET_BYTES, TILE_N, decode_slice_grid, expected_decode_plan,
+                   expected_decode_schedule, expected_plan, plan_cg)
 
 MS = (1, 5, 8, 9, 16, 17, 100, 128, 129, 300, 512, 1000, 1024, 4096, 8192)
-NS = (128, 640, 1024, 4096, 7168, 14336, 28672)
+NS = (128, 640, 1024, 4096, 7168, 14336, 18944, 19072, 28672)
 KS = (64, 448, 1024, 4096, 8192, 14336)
 BUDGETS = (0, 20 << 20, 1 << 40)
 
@@ -31,11 +31,7 @@ def test_plan_query_matches_the_mirrors(i4g, sms):
                 for budget in BUDGETS:
                     got = i4g.plan(M, N, K, 64, sms, budget)
                     if M <= 16:
-                        pref, grid, need = expected_decode_plan(M, N, K, sms=sms)
-                        if budget > 0 and pref and budget >= need:
-                            want = ("decode", "stream-k", grid, need)
-                        else:
-                            want = ("decode", "cluster", decode_cluster(N, K, sms), 0)
+                        want = ("decode",) + expected_decode_schedule(M, N, K, budget, sms=sms)
                     else:
                         kind, need, tile_m = expected_plan(M, N, K, budget=budget, sms=sms)
                         kern = f"tcgen05/{tile_m}"
@@ -66,8 +62,32 @@ def test_forced_decode_schedules(i4g):
         assert i4g.plan(4, 14336, 4096, 128, 148, need - 1)["schedule"] == "cluster"
         i4g.set_decode_schedule("cluster")
         assert i4g.plan(1, 28672, 8192, 128, 148, 1 << 40)["schedule"] == "cluster"
+        assert i4g.plan(1, 4096, 8192, 128, 148, 1 << 40)["schedule"] == "cluster"
+        # slices where N / 16 <= 8 x SMs; beyond that the cluster schedule
+        # (stream-K is never taken while slices are forced)
+        i4g.set_decode_schedule("slices")
+        assert i4g.plan(16, 18944, 8192, 64, 148, 0) == {
+            "kernel": "decode", "schedule": "slices", "param": 148, "workspace_bytes": 0}
+        assert i4g.plan(16, 19072, 8192, 64, 148, 1 << 40)["schedule"] == "cluster"
     finally:
         i4g.set_decode_schedule("auto")
+
+
+def test_slice_grid():
+    assert decode_slice_grid(128, 148) == 8            # one slice per CTA
+    assert decode_slice_grid(4096, 148) == 148         # one or two slices each
+    assert decode_slice_grid(148 * 8 * 16, 148) == 148  # eight each
+    assert decode_slice_grid(148 * 8 * 16 + 128, 148) == 0
+    assert decode_slice_grid(14336, 132) == 132
+
+
+def test_auto_takes_slices_where_possible(i4g):
+    for N, want in ((14336, "slices"), (4096, "slices"), (7168, "slices"), (28672, None)):
+        got = i4g.plan(4, N, 4096, 128, 148, 1 << 40)
+        if want:
+            assert got["schedule"] == want and got["param"] == 148, (N, got)
+        else:
+            assert got["schedule"] in ("stream-k", "cluster"), got
 
 
 def test_fp32_output_never_uses_the_decode_kernel(i4g):
