@@ -798,14 +798,16 @@ __global__ void __launch_bounds__(SL_THREADS, 1)
   }
   __syncthreads();
 
-  // Ring feeder: lane 0 of warp 0, which also computes (a separate producer
-  // warp would leave the 16-row instance too few registers). It issues
-  // stages 0 .. STAGES-1 up front and then, after its own part of stage i,
-  // refills the slot stage i-1 used (for stage i-1+STAGES) once every warp
-  // has released it; one stage of slack keeps it from waiting on the
-  // slowest warp's current stage.
-  const bool feeder = threadIdx.x == 0;
-  int issued = 0;   // stages issued so far (the feeder's count)
+  // Ring feeder: warp 0, which also computes (a separate producer warp
+  // would leave the 16-row instance too few registers); its lane 0 issues
+  // the copies. It issues stages 0 .. STAGES-1 up front and then, after its
+  // own part of stage i, refills the slot stage i-1 used (for stage
+  // i-1+STAGES) once every warp has released it; one stage of slack keeps it
+  // from waiting on the slowest warp's current stage. The whole warp takes
+  // these steps together: were lane 0 to wait alone, its 31 siblings spinning
+  // on the next stage's barrier could keep it from issuing that very stage.
+  const bool feeder = warp == 0;
+  int issued = 0;   // stages issued so far (same in every lane of warp 0)
   bool fed = true;  // false once the feeder gave up on a wait
   auto issue = [&](int i) {
     const int s = i % STAGES;
@@ -832,10 +834,14 @@ __global__ void __launch_bounds__(SL_THREADS, 1)
     }
   };
   if (feeder) {
-    prefetch_tensormap(&act_map);
-    prefetch_tensormap(&wmaps.box[n0 - 1]);
-    if (n1 > 0) prefetch_tensormap(&wmaps.box[n1 - 1]);
-    for (; issued < STAGES && issued < nstages; ++issued) issue(issued);
+    if (lane == 0) {
+      prefetch_tensormap(&act_map);
+      prefetch_tensormap(&wmaps.box[n0 - 1]);
+      if (n1 > 0) prefetch_tensormap(&wmaps.box[n1 - 1]);
+      for (int j = 0; j < STAGES && j < nstages; ++j) issue(j);
+    }
+    issued = min(STAGES, nstages);
+    __syncwarp();
   }
 
   // this warp's units: u = warp and warp + 16, u = slice * KPS + block
@@ -872,7 +878,9 @@ __global__ void __launch_bounds__(SL_THREADS, 1)
   for (int i = 0; i < nstages; ++i) {
     const int s = i % STAGES;
     const uint32_t ph = (i / STAGES) & 1u;
-    if (!mbar_wait(bars + 8 * s, ph, abort_flag, status, wait_limit_ns)) break;
+    // warp-uniform exit: every lane of a warp leaves at the same stage
+    if (!__all_sync(0xffffffffu, mbar_wait(bars + 8 * s, ph, abort_flag, status, wait_limit_ns)))
+      break;
     const uint32_t slot = ring + s * L::SLOT;
     const int kb = i * KPS;
     if (b < kblocks - kb) {
@@ -887,16 +895,22 @@ __global__ void __launch_bounds__(SL_THREADS, 1)
     if (lane == 0) mbar_arrive(bars + 8 * (STAGES + s));
     if (feeder && fed && i >= 1 && issued == i - 1 + STAGES && issued < nstages) {
       const int r = i - 1;
-      fed = mbar_wait(bars + 8 * (STAGES + r % STAGES), (r / STAGES) & 1u, abort_flag, status,
-                      wait_limit_ns);
-      if (fed) issue(issued++);
+      const bool ok = mbar_wait(bars + 8 * (STAGES + r % STAGES), (r / STAGES) & 1u, abort_flag,
+                                status, wait_limit_ns);
+      fed = __all_sync(0xffffffffu, ok);
+      if (fed) {
+        if (lane == 0) issue(issued);
+        ++issued;
+      }
+      __syncwarp();
     }
   }
-  if (feeder && *abort_flag) {
+  if (feeder && lane == 0 && *abort_flag) {
     // gave up: let the copies already issued land before the ring is reused
     for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; ++i)
       mbar_wait(bars + 8 * (i % STAGES), (i / STAGES) & 1u, never, nullptr, 100000000ull);
   }
+  __syncwarp();
   {
     // The four block-parts of each slice, added in order through shared
     // memory: the ring is reused once every warp has passed its last stage

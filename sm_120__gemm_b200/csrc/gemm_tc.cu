@@ -356,7 +356,7 @@ __device__ __forceinline__ void copies_epilogue(bool ok, const Outputs& out, int
       load_sum16(col0 + c * 16, &hb[c * 4], v);
       if (c == COLS / 16 - 1) {
         tc_fence_before();
-        if constexpr (CG == 2) mbar_arrive_cluster(empty_bar);  // the even CTA's barrier
+        if constexpr (CG == 2) mbar_arrive_cluster_relaxed(empty_bar);  // the even CTA's
         else mbar_arrive(empty_bar);
       }
 #pragma unroll
@@ -654,7 +654,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (uint32_t it = 0; it < total; ++it) {
         const int s = it % A_STAGES;
         if (!mbar_wait(afull(s), (it / A_STAGES) & 1u, abort_flag, status, wait_limit_ns)) break;
-        mbar_arrive_cluster(lead(afull(s)));
+        mbar_arrive_cluster_relaxed(lead(afull(s)));
       }
     }
     if (lane == 0) mbar_wait(drain_bar, 0, never, nullptr, 100000000ull);
@@ -712,7 +712,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       tmem_st_32x32b_x32(tmem_base + lane_addr + ts * T_COLS, r);
       tmem_st_wait();
       tc_fence_before();
-      if constexpr (PAIR) mbar_arrive_cluster(lead(tfull(ts)));
+      if constexpr (PAIR) mbar_arrive_cluster_relaxed(lead(tfull(ts)));
       else mbar_arrive(tfull(ts));
     }
   } else {
@@ -732,7 +732,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     constexpr int EPI_THREADS = NUM_EPI_WARPS * 32;
     auto release = [&](int acc) {
-      if constexpr (PAIR) mbar_arrive_cluster(lead(dempty(acc)));
+      if constexpr (PAIR) mbar_arrive_cluster_relaxed(lead(dempty(acc)));
       else mbar_arrive(dempty(acc));
     };
     auto wait_full = [&](int acc, uint32_t parity) {

@@ -255,56 +255,148 @@ __global__ void inverse_repack_umma_kernel(const uint32_t* __restrict__ tiles,
 inline unsigned blocks_for(size_t n) { return static_cast<unsigned>((n + THREADS - 1) / THREADS); }
 
 
+// quantize_one(x, s) for eight rows of two columns of a group, without a
+// division per element, for a scale s that is a finite normal FP16 number
+// (the caller takes quantize_one for the rest). Such an s is vmax / 7
+// rounded to FP16 (relative error <= 2^-11), so |x / s| <= 7.004 for every
+// x of the group and no code needs clamping. With r = 1/s rounded,
+// y = x * r is within 2^-20 of the quotient x / s and the rounded quotient
+// fl(x / s) within 2^-22 of it. n = y rounded to an integer by adding
+// 1.5 * 2^23 (ties to even; the low four bits of the sum are then n's code)
+// and d = y - n (exact); when |d| < 1/2 - 2^-18 the quotient and its
+// rounding lie strictly inside (n - 1/2, n + 1/2), so rint(fl(x / s)) = n.
+// Otherwise (within 2^-18 of a rounding tie, or x NaN) the element needs
+// quantize_one and codes8 returns false. Float pairs carry two columns.
+__device__ __forceinline__ bool codes8(const __half2 (&x)[8], float2 r, uint32_t& lo,
+                                       uint32_t& hi) {
+  const float2 magic = make_float2(12582912.0f, 12582912.0f);  // 1.5 * 2^23
+  const float2 neg_magic = make_float2(-12582912.0f, -12582912.0f);
+  const float2 minus_one = make_float2(-1.0f, -1.0f);
+  constexpr float kLim = 0.5f - 0x1p-18f;
+  uint32_t tl[8], th[8];
+  bool ok = true;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float2 y = __fmul2_rn(__half22float2(x[e]), r);
+    const float2 t = __fadd2_rn(y, magic);
+    const float2 d = __ffma2_rn(__fadd2_rn(t, neg_magic), minus_one, y);  // y - n
+    ok &= (fabsf(d.x) < kLim) & (fabsf(d.y) < kLim);
+    tl[e] = __float_as_uint(t.x);
+    th[e] = __float_as_uint(t.y);
+  }
+  // element e of a column sits at bit 4 (e / 2) + 16 (e % 2): bytes 0..3 of
+  // the word hold codes (e0, e2), (e4, e6), (e1, e3), (e5, e7) as low, high
+  // nibble; gather each code's low byte, then merge the two nibbles
+  auto pack = [](const uint32_t (&t)[8]) {
+    const uint32_t a = __byte_perm(__byte_perm(t[0], t[4], 0x0040), __byte_perm(t[1], t[5], 0x0040),
+                                   0x5410);
+    const uint32_t b = __byte_perm(__byte_perm(t[2], t[6], 0x0040), __byte_perm(t[3], t[7], 0x0040),
+                                   0x5410);
+    return (a & 0x0F0F0F0Fu) | ((b << 4) & 0xF0F0F0F0u);
+  };
+  lo = pack(tl);
+  hi = pack(th);
+  return ok;
+}
+
 // One pass from FP16 weights to the GEMM's inputs: a CTA reads a 128-column
 // x KC-row slab of B once (KC = max(64, group), whole groups and whole tile
 // blocks), computes the slab's scales exactly as quantize_kernel does, and
 // writes the codes straight into the tile layout of repack_umma_kernel and
 // the scales into the 128-column layout of repack_scales_128_kernel. Output
 // bytes are identical to quantize -> repack_umma + repack_scales_128.
+//
+// The slab sits in shared memory as rows of sixteen 16-byte chunks, chunk c
+// of row k stored at c ^ (2 ((k / 8) % 4)): the code pass reads rows k, k+8,
+// k+16, k+24 at once, which this spreads over all 32 banks.
 template <int GROUP>
 __global__ void __launch_bounds__(THREADS)
     quantize_repack_kernel(const __half* __restrict__ b, uint32_t* __restrict__ tiles,
                            __half* __restrict__ rscales, int K, int N) {
   constexpr int KC = GROUP > 64 ? GROUP : 64;
-  constexpr int GPC = KC / GROUP;  // groups per slab
-  __shared__ __align__(16) __half slab[KC][128];
-  __shared__ float sf[GPC][128];
+  constexpr int GPC = KC / GROUP;           // groups per slab
+  constexpr int P = THREADS / (64 * GPC);   // threads per (group, column pair)
+  constexpr int RPP = GROUP / P;            // rows each of them scans
+  static_assert(P >= 1 && (P & (P - 1)) == 0 && RPP >= 1, "scale pass split");
+  __shared__ __align__(16) __half slab[KC * 128];
+  __shared__ float sf[GPC][128];  // scales
+  __shared__ float sr[GPC][128];  // their rounded reciprocals; NaN: not a normal scale
   const int nt = blockIdx.x;
   const int kc = blockIdx.y;
   const int k0 = kc * KC;
+  auto chunk_at = [](int row, int ch) { return row * 128 + ((ch ^ (2 * ((row >> 3) & 3))) << 3); };
+  auto pair_at = [&](int row, int np) -> __half2 {
+    return *reinterpret_cast<const __half2*>(&slab[chunk_at(row, np >> 2) + 2 * (np & 3)]);
+  };
   // B rows k0..k0+KC, columns 128 nt..: 16 chunks of 16 bytes per row
-  for (int i = threadIdx.x; i < KC * 16; i += THREADS) {
+#pragma unroll
+  for (int j = 0; j < KC * 16 / THREADS; ++j) {
+    const int i = j * THREADS + threadIdx.x;
     const int r = i >> 4, ch = i & 15;
-    *reinterpret_cast<uint4*>(&slab[r][ch * 8]) = *reinterpret_cast<const uint4*>(
-        b + static_cast<size_t>(k0 + r) * N + static_cast<size_t>(nt) * 128 + ch * 8);
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(
+        b + static_cast<size_t>(k0 + r) * N + static_cast<size_t>(nt) * 128 + ch * 8));
+    *reinterpret_cast<uint4*>(&slab[chunk_at(r, ch)]) = v;
   }
   __syncthreads();
   const int groups = K / GROUP;
-  for (int i = threadIdx.x; i < GPC * 128; i += THREADS) {
-    const int gl = i >> 7, col = i & 127;
-    float vmax = 0.0f;
-    for (int r = gl * GROUP; r < (gl + 1) * GROUP; ++r)
-      vmax = max_like_std(vmax, fabsf(__half2float(slab[r][col])));
-    const __half sh = __float2half_rn(max_like_std(__fdiv_rn(vmax, 7.0f), 1.0e-8f));
-    rscales[(static_cast<size_t>(nt) * groups + kc * GPC + gl) * 128 + col] = sh;
-    sf[gl][col] = __half2float(sh);
+  {
+    // group abs-max of a column pair over RPP rows per thread, combined over
+    // the P adjacent lanes of the pair (the maximum ignores NaN, as the
+    // reference's std::max-style update does)
+    const int part = threadIdx.x % P;
+    const int np = (threadIdx.x / P) % 64;
+    const int gl = threadIdx.x / (P * 64);
+    __half2 m = __float2half2_rn(0.0f);
+    const int r0 = gl * GROUP + part * RPP;
+#pragma unroll 8
+    for (int r = r0; r < r0 + RPP; ++r) m = __hmax2(m, __habs2(pair_at(r, np)));
+#pragma unroll
+    for (int o = 1; o < P; o <<= 1) m = __hmax2(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float2 vmax = __half22float2(m);
+    const __half s0 = __float2half_rn(max_like_std(__fdiv_rn(vmax.x, 7.0f), 1.0e-8f));
+    const __half s1 = __float2half_rn(max_like_std(__fdiv_rn(vmax.y, 7.0f), 1.0e-8f));
+    if (part == 0) {
+      *reinterpret_cast<__half2*>(
+          &rscales[(static_cast<size_t>(nt) * groups + kc * GPC + gl) * 128 + 2 * np]) =
+          __halves2half2(s0, s1);
+      const float f0 = __half2float(s0), f1 = __half2float(s1);
+      const float kNaN = __int_as_float(0x7fffffff);
+      sf[gl][2 * np] = f0;
+      sf[gl][2 * np + 1] = f1;
+      sr[gl][2 * np] = (f0 >= 0x1p-14f && f0 <= 65504.0f) ? __frcp_rn(f0) : kNaN;
+      sr[gl][2 * np + 1] = (f1 >= 0x1p-14f && f1 <= 65504.0f) ? __frcp_rn(f1) : kNaN;
+    }
   }
   __syncthreads();
-  // tile-layout words of the slab's KC / 64 blocks: block [h][n][w], element
-  // k % 8 = 2p + hi at bit 4p + 16hi
+  // tile-layout words of the slab's KC / 64 blocks: block [h][n][w]; each
+  // thread makes the words of columns 2np and 2np + 1 (4 words apart)
   const int kblocks = K >> 6;
-  for (int i = threadIdx.x; i < (KC / 64) * 1024; i += THREADS) {
-    const int jb = i >> 10, wi = i & 1023;
-    const int h = wi >> 9, ni = (wi >> 2) & 127, w = wi & 3;
+#pragma unroll 1
+  for (int i = threadIdx.x; i < (KC / 64) * 512; i += THREADS) {
+    const int jb = i >> 9, rr = i & 511;
+    const int h = rr >> 8, np = (rr >> 2) & 63, w = rr & 3;
     const int kk0 = jb * 64 + h * 32 + w * 8;  // row inside the slab
-    const float sc = sf[kk0 / GROUP][ni];
-    uint32_t word = 0;
+    const int gl = kk0 / GROUP;
+    __half2 x[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int q = quantize_one(__half2float(slab[kk0 + e][ni]), sc);
-      word |= static_cast<uint32_t>(q & 15) << (4 * (e >> 1) + 16 * (e & 1));
+    for (int e = 0; e < 8; ++e) x[e] = pair_at(kk0 + e, np);
+    uint32_t lo, hi;
+    // a NaN reciprocal (scale not a finite normal number) makes every d NaN
+    if (!codes8(x, make_float2(sr[gl][2 * np], sr[gl][2 * np + 1]), lo, hi)) {
+      const float f0 = sf[gl][2 * np], f1 = sf[gl][2 * np + 1];
+      lo = hi = 0u;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int sh = 4 * (e >> 1) + 16 * (e & 1);
+        const float2 v = __half22float2(x[e]);
+        lo |= static_cast<uint32_t>(quantize_one(v.x, f0) & 15) << sh;
+        hi |= static_cast<uint32_t>(quantize_one(v.y, f1) & 15) << sh;
+      }
     }
-    tiles[(static_cast<size_t>(nt) * kblocks + kc * (KC / 64) + jb) * 1024 + wi] = word;
+    uint32_t* dst = tiles + (static_cast<size_t>(nt) * kblocks + kc * (KC / 64) + jb) * 1024 +
+                    h * 512 + (2 * np) * 4 + w;
+    dst[0] = lo;
+    dst[4] = hi;
   }
 }
 

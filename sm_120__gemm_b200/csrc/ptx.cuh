@@ -218,6 +218,16 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
                : "memory");
 }
 
+// Arrival on a cluster CTA's barrier without release semantics (no fence
+// before it). For signals that follow work the thread has already seen
+// complete: tcgen05.wait::st / wait::ld for TMEM, a complete_tx barrier for a
+// TMA copy into shared memory. The waiter's acquire plus
+// tcgen05.fence::after_thread_sync then orders its own tcgen05 work after.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(

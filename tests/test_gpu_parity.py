@@ -284,7 +284,8 @@ def test_wait_timeout_is_reported_not_faulted(i4g):
 
 def special_weights(K, N, seed):
     """N(0, 0.02) weights with the quantiser's edge cases planted: an all-zero
-    group, subnormal and tie values, +-65504 and a lone large outlier."""
+    group, subnormal and tie values, +-65504, a lone large outlier and
+    columns of exact rounding ties."""
     g = torch.Generator().manual_seed(seed)
     w = torch.randn(K, N, generator=g) * 0.02
     w[0:32, 0] = 0.0
@@ -293,6 +294,11 @@ def special_weights(K, N, seed):
     w[5, 3] = 65504.0
     w[6, 3] = -65504.0
     w[7, 4] = 1.0e4
+    # exact rounding ties: scale 0.75 with x = +-(k + 0.5) * 0.75, scale 1
+    # with x = k / 2
+    pattern = [5.25] + [(-1) ** k * (k + 0.5) * 0.75 for k in range(7)]
+    w[:, 7] = torch.tensor([pattern[i % len(pattern)] for i in range(K)])
+    w[:, 8] = torch.tensor([((i % 29) - 14) * 0.5 for i in range(K)])
     return w.half()
 
 
