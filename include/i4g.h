@@ -264,12 +264,14 @@ int i4g_plan(int M, int N, int K, int group, int fp32_out, int sm_count,
              size_t workspace_bytes, int* kernel, int* schedule, int* param,
              size_t* bytes);
 
-/* The tcgen05 kernel runs 256-row tiles on CTA pairs (thread-block clusters
- * of two, one 2-SM tensor-core instruction per pair) when N % 256 == 0.
- * i4g_plan assumes sm_count / 2 pairs resident at once; launches on a device
- * use the number of pairs that fit on it (clusters are placed within GPCs),
- * which i4g_max_pairs reports for the current device. WHOLE schedules report
- * the grid in CTAs; the I4G_PAIR=0 environment variable keeps single CTAs. */
+/* With the I4G_PAIR=1 environment variable (read at the first launch) the
+ * tcgen05 kernel runs 256-row tiles on CTA pairs (thread-block clusters of
+ * two, one 2-SM tensor-core instruction per pair) when N % 256 == 0, with
+ * whole-tile or equal-split tails (no stream-K); by default it runs single
+ * CTAs, which are as fast. i4g_plan assumes sm_count / 2 pairs resident at
+ * once; launches on a device use the number of pairs that fit on it
+ * (clusters are placed within GPCs), which i4g_max_pairs reports for the
+ * current device. WHOLE schedules report the grid in CTAs. */
 int i4g_max_pairs(int* pairs);
 
 /* ---- kernel registry queries (include/kernels.cuh:6-22, 85-105) ---------- */

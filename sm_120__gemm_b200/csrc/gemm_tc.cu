@@ -919,14 +919,15 @@ constexpr double kSplitUs = 12.0, kStreamKUs = 20.0;
 int pair_mode() {
   static const int v = [] {
     const char* e = std::getenv("I4G_PAIR");
-    return e ? std::atoi(e) : 1;
+    return e ? std::atoi(e) : 0;
   }();
   return v;
 }
 
 int choose_cg(int tile_m, int N, int sm_count) {
   // CTA pairs for the 256-row tiles when the weight columns split into
-  // 256-column pair tiles (I4G_PAIR=0 keeps single CTAs).
+  // 256-column pair tiles, with I4G_PAIR=1 (single CTAs by default: pairs run
+  // no faster on B200 here).
   return (pair_mode() != 0 && tile_m == 256 && N % 256 == 0 && sm_count >= 2) ? 2 : 1;
 }
 
@@ -997,9 +998,11 @@ Plan make_plan(int tile_m, int M, int N, int K, int sm_count, size_t budget,
     p.grid = cg * (p.sched.items < units ? p.sched.items : units);
     p.workspace_bytes = split_bytes;
   }
-  if (allow_stream_k) {
+  if (allow_stream_k && cg == 1) {
     // equal shares of the tail's blocks, one per unit: at least eight blocks
-    // each, at most four shares per tile, more shares than tiles
+    // each, at most four shares per tile, more shares than tiles (single
+    // CTAs only: on pairs this tail gave wrong odd-CTA half tiles now and
+    // then, a race not yet found, so pairs keep whole tiles and equal splits)
     const long run = static_cast<long>(rem) * kblocks;
     int chunks = units;
     chunks = chunks < 3 * rem ? chunks : 3 * rem;

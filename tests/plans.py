@@ -25,8 +25,11 @@ def device_pairs():
 
 
 def plan_cg(tile_m, N):
-    """CTAs per tile: 2 (a CTA pair) for 256-row tiles of N % 256 == 0."""
-    return 2 if tile_m == 256 and N % 256 == 0 else 1
+    """CTAs per tile: 2 (a CTA pair) for 256-row tiles of N % 256 == 0 when
+    I4G_PAIR=1 is set, else 1."""
+    import os
+    pairs_on = os.environ.get("I4G_PAIR", "0") not in ("", "0")
+    return 2 if pairs_on and tile_m == 256 and N % 256 == 0 else 1
 
 
 def expected_plan(M, N, K, budget=1 << 62, sms=None, pairs=None):
@@ -54,7 +57,7 @@ def expected_plan(M, N, K, budget=1 << 62, sms=None, pairs=None):
         best, plan = (waves + 1.0 / f) * t_tile + 12.0, (f"split{f}", need, tile_m)
     run = rem * kb
     chunks = min(units, 3 * rem, run // 8)
-    if chunks > rem:
+    if chunks > rem and cg == 1:
         most = max((((t + 1) * kb) * chunks - 1) // run - ((t * kb + 1) * chunks - 1) // run + 1
                    for t in range(rem))
         need = TICKET_BYTES + (rem + chunks - 1) * tile_bytes
