@@ -313,11 +313,11 @@ int i4g_kernel_resources(int variant, int rows, int group, i4g_kernel_resources_
  * through distributed shared memory; needs no workspace) and the stream-K
  * schedule of the *_ws entry points (see the workspace section). AUTO (the
  * default, or the I4G_DECODE_SCHEDULE environment variable's "slices" /
- * "cluster" / "streamk" at the first call) takes the slice schedule where it
- * is possible, else stream-K when it takes enough work off the busiest SM to
- * pay for its reduction through global memory, else the cluster schedule;
- * the others force one (slices where possible, stream-K only where a large
- * enough workspace is given, the cluster schedule otherwise).
+ * "cluster" / "streamk" at the first call) takes stream-K when it takes
+ * enough work off the busiest SM to pay for its reduction through global
+ * memory, else the cluster schedule (the slice schedule measured slower on
+ * every shape); the others force one (slices where possible, stream-K only
+ * where a large enough workspace is given, the cluster schedule otherwise).
  * Process-wide; affects launches issued after the call. */
 enum {
   I4G_DECODE_AUTO = 0,

@@ -192,64 +192,6 @@ int act_map(const void* A, int M, int K, int rows, const CUtensorMap** out) {
   return I4G_OK;
 }
 
-// The decode slice schedule's weight tensor maps over one weight buffer
-// ({256 bytes, 8 slices, 2 halves, K/64 blocks, N/128 tiles}, strides 256,
-// 2048, 4096 and (K/64) * 4096 bytes; map n-1 has a box of n slices x 2
-// halves x 4 blocks). Cached per host thread like the activation maps.
-struct SliceMapEntry {
-  int device = -1;
-  const void* tiles = nullptr;
-  int N = 0, K = 0;
-  unsigned long long used = 0;
-  i4g::dec::SliceMaps maps;
-};
-
-int slice_maps(const void* tiles, int N, int K, const i4g::dec::SliceMaps** out) {
-  constexpr int kEntries = 4;
-  thread_local SliceMapEntry cache[kEntries];
-  thread_local unsigned long long clock = 0;
-  int dev = -1;
-  cudaGetDevice(&dev);
-  ++clock;
-  SliceMapEntry* victim = &cache[0];
-  for (SliceMapEntry& e : cache) {
-    if (e.device == dev && e.tiles == tiles && e.N == N && e.K == K) {
-      e.used = clock;
-      *out = &e.maps;
-      return I4G_OK;
-    }
-    if (e.used < victim->used) victim = &e;
-  }
-  EncodeTiledFn encode = nullptr;
-  int st = encode_fn(&encode);
-  if (st != I4G_OK) return st;
-  const cuuint64_t dims[5] = {256, 8, 2, static_cast<cuuint64_t>(K / 64),
-                              static_cast<cuuint64_t>(N / 128)};
-  const cuuint64_t strides[4] = {256, 2048, 4096, static_cast<cuuint64_t>(K / 64) * 4096};
-  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-  for (int n = 1; n <= i4g::dec::kSliceMax; ++n) {
-    const cuuint32_t box[5] = {256, static_cast<cuuint32_t>(n), 2, 4, 1};
-    const CUresult r = encode(&victim->maps.box[n - 1], CU_TENSOR_MAP_DATA_TYPE_UINT8, 5,
-                              const_cast<void*>(tiles), dims, strides, box, estr,
-                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) {
-      victim->device = -1;
-      victim->used = 0;
-      return fail(I4G_ERR_DRIVER, "cuTensorMapEncodeTiled (weight slices) failed with CUresult %d",
-                  int(r));
-    }
-  }
-  victim->device = dev;
-  victim->tiles = tiles;
-  victim->N = N;
-  victim->K = K;
-  victim->used = clock;
-  *out = &victim->maps;
-  return I4G_OK;
-}
-
 unsigned long long g_wait_limit_ns = kDefaultWaitLimitNs;
 
 using MemRangeFn = int (*)(unsigned long long*, size_t*, unsigned long long);
@@ -341,13 +283,8 @@ int gemm_common(const void* A, const uint8_t* tiles, const void* scales, const i
     const CUtensorMap* dmap = nullptr;
     st = act_map(A, M, K, -i4g::dec::rows_for(M), &dmap);
     if (st != I4G_OK) return st;
-    const i4g::dec::SliceMaps* smaps = nullptr;
-    if (i4g::dec::pick_schedule(M, N, K, dev->sm_count, workspace ? workspace_bytes : 0) ==
-        i4g::dec::kScheduleSlices) {
-      st = slice_maps(tiles, N, K, &smaps);
-      if (st != I4G_OK) return st;
-    }
-    return finish(i4g::dec::launch(*dmap, smaps, tiles, sc, out, M, N, K, group, dev->sm_count,
+    return finish(i4g::dec::launch(*dmap, static_cast<const __half*>(A), tiles, sc, out, M, N, K,
+                                   group, dev->sm_count,
                                    workspace, workspace ? workspace_bytes : 0,
                                    dev->status_word, g_wait_limit_ns, s),
                   "decode kernel launch");

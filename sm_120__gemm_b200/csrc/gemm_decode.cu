@@ -690,49 +690,59 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM)
 // A operand each) and CTA c (one per SM) owns the contiguous run of slices
 // [c*S/G, (c+1)*S/G) over all of K, so no two CTAs share an output and
 // nothing is reduced across CTAs, and every SM streams the same number of
-// weight bytes to within one slice. A run spans at most two 128-column tiles
-// of the layout; per ring stage (four 64-k blocks) one thread fetches each
-// tile segment's slices with one 5-D TMA box ({256 bytes of a slice-half,
-// slices, 2 halves, 4 blocks}), its scale groups with one bulk copy, and
-// the activation rows with the 3-D box of the other schedules. Sixteen
-// warps take the stage's (slice, block) units round robin, unit u =
-// slice * 4 + block going to warp u % 16, so the four SMSPs get equal
-// shares; each warp keeps the sums of its (slice, block-of-stage) units over
-// all stages, and at the end the four block-parts of each slice are added in
-// order through shared memory (deterministic).
+// weight bytes to within one slice. A stage is BS 64-k blocks (BS = 16, 8
+// or 4 for runs of at most 2, 4 or 8 slices, so that the run's (slice,
+// block) units give each of the 16 warps one or two); unit u goes to warp
+// u % 16. Every thread also fetches a share of each stage with 16-byte
+// cp.async copies (the activation rows into the 128-byte-swizzled layout
+// the block step reads, the run's slice-halves and the run's columns of the
+// stage's scale groups) and signals the stage's barrier once they land:
+// small copies through the copy engine (a 5-D tensor box of 256-byte lines,
+// or 256-byte bulk copies) were served one after another, about a stage per
+// half microsecond. Each warp keeps the sums of its units over all stages;
+// at the end the block-parts of each slice are added in order through
+// shared memory (deterministic).
 
 constexpr int SLICE_COLS = 16;
-constexpr int SL_WARPS = 16;                      // all of them compute
+constexpr int SL_WARPS = 16;
 constexpr int SL_THREADS = SL_WARPS * 32;
-constexpr int SL_MAX = 8;                         // slices a CTA may own
-constexpr int SL_UNITS = SL_MAX * KPS;            // (slice, block) units per stage, at most
-
-using SliceMaps = ::i4g::dec::SliceMaps;
+constexpr int SL_MAX = 8;  // slices a CTA may own
 static_assert(SL_MAX == kSliceMax, "slice bound");
 
-template <int MT, int GROUP, int STAGES>
+// Blocks per stage for a run of at most `nsl` slices.
+constexpr int slice_bs(int nsl) { return nsl <= 2 ? 16 : nsl <= 4 ? 8 : 4; }
+
+template <int MT, int GROUP, int BS>
 struct SliceLayout {
   static constexpr int ROWS = MT * 8;
-  static constexpr int ABYTES = KPS * ROWS * BK * 2;      // activation box, swizzled
-  static constexpr int WBYTES = SL_MAX * KPS * 2 * 256;   // up to eight slices
-  static constexpr int SGROUPS = KPS * BK / GROUP + (GROUP > BK ? 1 : 0);
-  static constexpr int SBYTES = 2 * SGROUPS * 256;        // up to two tile segments
+  static constexpr int NSL = BS == 16 ? 2 : BS == 8 ? 4 : 8;  // slices at most
+  static constexpr int ABYTES = BS * ROWS * 128;              // [block][row][64 k], swizzled
+  static constexpr int WBYTES = NSL * BS * 512;               // [block][half][slice][256 B]
+  static constexpr int SG = BS * BK / GROUP;                  // scale groups per stage
+  static constexpr int SBYTES = SG * NSL * 32;                // [group][slice][16 columns]
   static constexpr int SLOT = ((ABYTES + WBYTES + SBYTES + 1023) / 1024) * 1024;
-  static constexpr int BARS = STAGES * SLOT;              // full[], empty[]
-  static constexpr int ABORT = BARS + 2 * STAGES * 8;
-  static constexpr int DYN = ABORT + 16 + 1024;
-  // the final cross-warp sums reuse the ring: [unit][lane][MT * 4] floats
-  static_assert(SL_UNITS * 32 * MT * 4 * 4 <= BARS, "reduction scratch fits the ring");
+  static constexpr int UNITS = NSL * BS;                      // (slice, block) units, <= 32
+  static_assert(UNITS <= 2 * SL_WARPS, "two units per warp at most");
+  static_assert(BK * BS % GROUP == 0, "stages hold whole scale groups");
 };
 
-template <int MT, int GROUP>
+template <int MT, int GROUP, int BS>
 constexpr int slice_stages() {
+  using L = SliceLayout<MT, GROUP, BS>;
   int s = 8;
-  while (s > 2 && SliceLayout<MT, GROUP, 8>::SLOT * s + 2 * s * 8 + 16 + 1024 + 1024 >
-                      SMEM_PER_SM)
-    --s;
+  while (s > 2 && L::SLOT * s + 2 * s * 8 + 16 + 1024 + 1024 > SMEM_PER_SM) --s;
   return s;
 }
+
+template <int MT, int GROUP, int BS, int STAGES>
+struct SliceRing {
+  using L = SliceLayout<MT, GROUP, BS>;
+  static constexpr int BARS = STAGES * L::SLOT;  // full[STAGES]
+  static constexpr int ABORT = BARS + STAGES * 8;
+  static constexpr int DYN = ABORT + 16 + 1024;
+  // the final cross-warp sums reuse the ring: [unit][lane][MT] float4
+  static_assert(L::UNITS * 32 * MT * 16 <= BARS, "reduction scratch fits the ring");
+};
 
 // Writes one lane's four sums of the fragment of slice column base `col`
 // (16 columns) and row block mb to every copy of C (as store_fragment).
@@ -758,20 +768,27 @@ __device__ __forceinline__ void store_slice_fragment(const Outputs& out, int M, 
   }
 }
 
-template <int MT, int GROUP, int STAGES>
+// Scale group, inside a stage, of lane (., t)'s 16 k of block b.
+template <int GROUP>
+__device__ __forceinline__ int slice_group(int b, int t) {
+  if constexpr (GROUP == 32) return 2 * b + (t >> 1);
+  if constexpr (GROUP == 64) return b;
+  return b >> 1;
+}
+
+template <int MT, int GROUP, int BS, int STAGES>
 __global__ void __launch_bounds__(SL_THREADS, 1)
-    decode_slices_kernel(const __grid_constant__ CUtensorMap act_map,
-                         const __grid_constant__ SliceMaps wmaps,
+    decode_slices_kernel(const __half* __restrict__ A, const uint8_t* __restrict__ tiles,
                          const __half* __restrict__ scales, const __grid_constant__ Outputs out,
                          int M, int N, int K, int* status, unsigned long long wait_limit_ns) {
-  using L = SliceLayout<MT, GROUP, STAGES>;
+  using L = SliceLayout<MT, GROUP, BS>;
+  using R = SliceRing<MT, GROUP, BS, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const uint32_t ring = smem_u32(smem);
-  const uint32_t bars = ring + L::BARS;  // full[STAGES], empty[STAGES]
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::ABORT);
-  volatile int* never = abort_flag + 2;  // a flag nobody sets (draining waits)
+  const uint32_t bars = ring + R::BARS;  // full[STAGES]
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + R::ABORT);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -780,92 +797,74 @@ __global__ void __launch_bounds__(SL_THREADS, 1)
   const int nslices = N / SLICE_COLS;
   const int s0 = static_cast<int>((static_cast<long>(blockIdx.x) * nslices) / gridDim.x);
   const int s1 = static_cast<int>((static_cast<long>(blockIdx.x + 1) * nslices) / gridDim.x);
-  const int nsl = s1 - s0;                         // 1 .. SL_MAX (host-checked)
-  const int tile0 = s0 / 8;
-  const int n0 = min(nsl, 8 - s0 % 8);             // slices in the first tile segment
-  const int n1 = nsl - n0;                         // in the next tile
-  const int nstages = (kblocks + KPS - 1) / KPS;
+  const int nsl = s1 - s0;  // 1 .. L::NSL (host-checked)
+  const int nstages = (kblocks + BS - 1) / BS;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(bars + 8 * s, 1);
-      mbar_init(bars + 8 * (STAGES + s), SL_WARPS);
-    }
+    // every thread arrives once per stage, when its copies have landed
+    for (int s = 0; s < STAGES; ++s) mbar_init(bars + 8 * s, SL_THREADS);
     *abort_flag = 0;
-    *never = 0;
     fence_mbarrier_init();
-    fence_proxy_async_smem();
   }
   __syncthreads();
 
-  // Ring feeder: warp 0, which also computes (a separate producer warp
-  // would leave the 16-row instance too few registers); its lane 0 issues
-  // the copies. It issues stages 0 .. STAGES-1 up front and then, after its
-  // own part of stage i, refills the slot stage i-1 used (for stage
-  // i-1+STAGES) once every warp has released it; one stage of slack keeps it
-  // from waiting on the slowest warp's current stage. The whole warp takes
-  // these steps together: were lane 0 to wait alone, its 31 siblings spinning
-  // on the next stage's barrier could keep it from issuing that very stage.
-  const bool feeder = warp == 0;
-  int issued = 0;   // stages issued so far (same in every lane of warp 0)
-  bool fed = true;  // false once the feeder gave up on a wait
+  // This thread's copies of stage i: 16-byte pieces p = threadIdx.x + 512 n
+  // of [activation: block, row, chunk][weights: block, half, slice, chunk]
+  // [scales: group, slice, half-slice].
+  const int apieces = BS * L::ROWS * 8;
+  const size_t act_row = static_cast<size_t>(K);
   auto issue = [&](int i) {
-    const int s = i % STAGES;
-    const int kb = i * KPS;
-    const int nkb = min(KPS, kblocks - kb);
-    const int g0 = kb * BK / GROUP;
-    const int g1 = ((kb + nkb) * BK + GROUP - 1) / GROUP;
-    const uint32_t slot = ring + s * L::SLOT;
-    const uint32_t full = bars + 8 * s;
-    // full boxes count even where they reach past K (zero fill)
-    mbar_arrive_expect_tx(full, L::ABYTES + nsl * KPS * 2 * 256 +
-                                    (n1 > 0 ? 2 : 1) * (g1 - g0) * 256);
-    tma_load_3d(slot, &act_map, full, 0, 0, kb);
-    const uint32_t w0 = slot + L::ABYTES;
-    tma_load_5d(w0, &wmaps.box[n0 - 1], full, 0, s0 % 8, 0, kb, tile0);
-    const uint32_t sdst = slot + L::ABYTES + L::WBYTES;
-    bulk_load(sdst, scales + (static_cast<size_t>(tile0) * groups + g0) * 128, (g1 - g0) * 256,
-              full);
-    if (n1 > 0) {
-      tma_load_5d(w0 + n0 * KPS * 2 * 256, &wmaps.box[n1 - 1], full, 0, 0, 0, kb, tile0 + 1);
-      bulk_load(sdst + L::SGROUPS * 256,
-                scales + (static_cast<size_t>(tile0 + 1) * groups + g0) * 128, (g1 - g0) * 256,
-                full);
+    const uint32_t slot = ring + (i % STAGES) * L::SLOT;
+    const int kb = i * BS;
+    const int nkb = min(BS, kblocks - kb);
+    const int wpieces = nkb * 2 * nsl * 16;
+    const int spieces = (nkb * BK / GROUP) * nsl * 2;
+    const int total = apieces + wpieces + spieces;
+    for (int p = threadIdx.x; p < total; p += SL_THREADS) {
+      if (p < apieces) {
+        const int blk = p / (L::ROWS * 8), r = (p >> 3) % L::ROWS, c = p & 7;
+        const bool valid = r < M && blk < nkb;
+        const __half* src = valid ? A + r * act_row + (kb + blk) * BK + c * 8 : A;
+        cp_async16(slot + (blk * L::ROWS + r) * 128 + ((c ^ (r & 7)) << 4), src, valid ? 16 : 0);
+      } else if (p < apieces + wpieces) {
+        const int q = p - apieces;
+        const int c = q & 15, j = (q >> 4) % nsl, bh = (q >> 4) / nsl;  // bh = block * 2 + half
+        const int sl = s0 + j;
+        const uint8_t* src = tiles +
+                             (static_cast<size_t>(sl >> 3) * kblocks + kb + (bh >> 1)) * 4096 +
+                             (bh & 1) * 2048 + (sl & 7) * 256 + c * 16;
+        cp_async16(slot + L::ABYTES + (bh * nsl + j) * 256 + c * 16, src, 16);
+      } else {
+        const int q = p - apieces - wpieces;
+        const int h = q & 1, j = (q >> 1) % nsl, gi = (q >> 1) / nsl;
+        const int sl = s0 + j;
+        const __half* src = scales +
+                            (static_cast<size_t>(sl >> 3) * groups + kb * BK / GROUP + gi) * 128 +
+                            (sl & 7) * SLICE_COLS + h * 8;
+        cp_async16(slot + L::ABYTES + L::WBYTES + (gi * nsl + j) * 32 + h * 16, src, 16);
+      }
     }
+    cp_async_arrive(bars + 8 * (i % STAGES));
   };
-  if (feeder) {
-    if (lane == 0) {
-      prefetch_tensormap(&act_map);
-      prefetch_tensormap(&wmaps.box[n0 - 1]);
-      if (n1 > 0) prefetch_tensormap(&wmaps.box[n1 - 1]);
-      for (int j = 0; j < STAGES && j < nstages; ++j) issue(j);
-    }
-    issued = min(STAGES, nstages);
-    __syncwarp();
-  }
+  for (int i = 0; i < STAGES && i < nstages; ++i) issue(i);
 
-  // this warp's units: u = warp and warp + 16, u = slice * KPS + block
+  // this warp's units: u = warp and warp + 16, u = slice * BS + block (the
+  // same block for both)
   const int g = lane >> 2, t = lane & 3;
   const uint32_t a0 = g * 128 + (((2 * t) ^ g) << 4);
   const uint32_t a1 = g * 128 + (((2 * t + 1) ^ g) << 4);
-  const int b = warp % KPS;  // the block of the stage both units take
+  const int b = warp % BS;
+  const uint32_t aoff = b * (L::ROWS * 128);
   uint32_t woff[2], soff[2];
   bool own[2];
 #pragma unroll
   for (int q = 0; q < 2; ++q) {
     const int u = warp + q * SL_WARPS;
-    own[q] = u < nsl * KPS;
-    const int j = own[q] ? u / KPS : 0;
-    const bool second = j >= n0;
-    const int jl = second ? j - n0 : j;
-    const int ns = second ? n1 : n0;
-    // [block][half][slice][16 columns x 16 bytes] per tile segment
-    woff[q] = L::ABYTES + (second ? n0 * KPS * 2 * 256 : 0) + ((b * 2 + (t >> 1)) * ns + jl) * 256 +
-              g * 16 + (t & 1) * 8;
-    soff[q] = L::ABYTES + L::WBYTES + (second ? L::SGROUPS * 256 : 0) +
-              (((s0 + j) % 8) * SLICE_COLS + g) * 2;
+    own[q] = u < nsl * BS;
+    const int j = own[q] ? u / BS : 0;
+    woff[q] = L::ABYTES + ((b * 2 + (t >> 1)) * nsl + j) * 256 + g * 16 + (t & 1) * 8;
+    soff[q] = L::ABYTES + L::WBYTES + (slice_group<GROUP>(b, t) * nsl + j) * 32 + g * 2;
   }
-  const uint32_t aoff = b * (L::ROWS * 128);
   float acc[2][MT][4][4];
 #pragma unroll
   for (int q = 0; q < 2; ++q)
@@ -877,46 +876,25 @@ __global__ void __launch_bounds__(SL_THREADS, 1)
         for (int y = 0; y < 4; ++y) acc[q][mb][x][y] = 0.0f;
   for (int i = 0; i < nstages; ++i) {
     const int s = i % STAGES;
-    const uint32_t ph = (i / STAGES) & 1u;
-    // warp-uniform exit: every lane of a warp leaves at the same stage
-    if (!__all_sync(0xffffffffu, mbar_wait(bars + 8 * s, ph, abort_flag, status, wait_limit_ns)))
-      break;
+    const bool ok = mbar_wait(bars + 8 * s, (i / STAGES) & 1u, abort_flag, status, wait_limit_ns);
+    // uniform exit; past this barrier every thread is done with stage i - 1,
+    // whose slot takes stage i - 1 + STAGES
+    if (!__syncthreads_and(ok)) break;
+    if (i >= 1 && i - 1 + STAGES < nstages) issue(i - 1 + STAGES);
     const uint32_t slot = ring + s * L::SLOT;
-    const int kb = i * KPS;
-    if (b < kblocks - kb) {
-      const uint32_t so = scale_offset<GROUP>(b, t, kb & 1);
+    if (b < kblocks - i * BS) {
 #pragma unroll
       for (int q = 0; q < 2; ++q)
         if (own[q])
-          block_step(slot + woff[q], slot + soff[q] + so, slot + a0 + aoff, slot + a1 + aoff,
-                     acc[q]);
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(bars + 8 * (STAGES + s));
-    if (feeder && fed && i >= 1 && issued == i - 1 + STAGES && issued < nstages) {
-      const int r = i - 1;
-      const bool ok = mbar_wait(bars + 8 * (STAGES + r % STAGES), (r / STAGES) & 1u, abort_flag,
-                                status, wait_limit_ns);
-      fed = __all_sync(0xffffffffu, ok);
-      if (fed) {
-        if (lane == 0) issue(issued);
-        ++issued;
-      }
-      __syncwarp();
+          block_step(slot + woff[q], slot + soff[q], slot + a0 + aoff, slot + a1 + aoff, acc[q]);
     }
   }
-  if (feeder && lane == 0 && *abort_flag) {
-    // gave up: let the copies already issued land before the ring is reused
-    for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; ++i)
-      mbar_wait(bars + 8 * (i % STAGES), (i / STAGES) & 1u, never, nullptr, 100000000ull);
-  }
-  __syncwarp();
+  // every copy has landed (or, after a timeout, lands now) before the ring
+  // is reused
+  cp_async_wait_all();
+  __syncthreads();
   {
-    // The four block-parts of each slice, added in order through shared
-    // memory: the ring is reused once every warp has passed its last stage
-    // (every copy had landed for it to do so, or was drained above).
-    constexpr int CTHREADS = SL_WARPS * 32;
-    epi_bar_sync(CTHREADS);
+    // The block-parts of each slice, added in order through shared memory.
     float4* red = reinterpret_cast<float4*>(smem);  // [unit][lane][MT]
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
@@ -932,17 +910,17 @@ __global__ void __launch_bounds__(SL_THREADS, 1)
         red[(u * 32 + lane) * MT + mb] = v;
       }
     }
-    epi_bar_sync(CTHREADS);
+    __syncthreads();
     // thread -> (slice j, lane ln, row block mb)
     const int idx = static_cast<int>(threadIdx.x);
     const int j = idx / (32 * MT);
     const int ln = (idx / MT) % 32;
     const int mb = idx % MT;
     if (j < nsl) {
-      float4 sum = red[((j * KPS) * 32 + ln) * MT + mb];
+      float4 sum = red[((j * BS) * 32 + ln) * MT + mb];
 #pragma unroll
-      for (int bb = 1; bb < KPS; ++bb) {
-        const float4 v = red[((j * KPS + bb) * 32 + ln) * MT + mb];
+      for (int bb = 1; bb < BS; ++bb) {
+        const float4 v = red[((j * BS + bb) * 32 + ln) * MT + mb];
         sum.x += v.x;
         sum.y += v.y;
         sum.z += v.z;
@@ -1034,11 +1012,11 @@ int choose_cluster(int N, int K, int sm_count) {
   return best;
 }
 
-// Schedule choice: kScheduleAuto takes the slice schedule where slice_grid
-// allows it, else lets the model in sk_plan decide between stream-K and the
-// cluster schedule; kScheduleSlices / kScheduleCluster / kScheduleStreamK
-// force one (slices where possible, stream-K only with a large enough
-// workspace). Set by set_schedule; until then, I4G_DECODE_SCHEDULE
+// Schedule choice: kScheduleAuto lets the model in sk_plan decide between
+// stream-K and the cluster schedule (the slice schedule is slower on every
+// measured shape); kScheduleSlices / kScheduleCluster / kScheduleStreamK
+// force one (slices where slice_grid allows, stream-K only with a large
+// enough workspace). Set by set_schedule; until then, I4G_DECODE_SCHEDULE
 // ("slices", "cluster" or "streamk") gives the initial value.
 std::atomic<int> g_schedule{-1};
 
@@ -1092,20 +1070,38 @@ SkPlan sk_plan(int M, int N, int K, int sm_count) {
   return p;
 }
 
-template <int MT, int GROUP>
-cudaError_t launch_slices_typed(const CUtensorMap& act_map, const SliceMaps& maps,
-                                const __half* scales, const Outputs& out, int M, int N, int K,
-                                int grid, int* status, unsigned long long wait_limit_ns,
-                                cudaStream_t stream) {
-  constexpr int S = slice_stages<MT, GROUP>();
-  using L = SliceLayout<MT, GROUP, S>;
-  auto kernel = decode_slices_kernel<MT, GROUP, S>;
+template <int MT, int GROUP, int BS>
+cudaError_t launch_slices_typed(const __half* A, const uint8_t* tiles, const __half* scales,
+                                const Outputs& out, int M, int N, int K, int grid, int* status,
+                                unsigned long long wait_limit_ns, cudaStream_t stream) {
+  constexpr int S = slice_stages<MT, GROUP, BS>();
+  using R = SliceRing<MT, GROUP, BS, S>;
+  auto kernel = decode_slices_kernel<MT, GROUP, BS, S>;
   static std::atomic<uint64_t> configured{0};  // devices set, per instantiation
-  cudaError_t e = ensure_dynamic_smem(kernel, L::DYN, configured);
+  cudaError_t e = ensure_dynamic_smem(kernel, R::DYN, configured);
   if (e != cudaSuccess) return e;
-  kernel<<<grid, SL_THREADS, L::DYN, stream>>>(act_map, maps, scales, out, M, N, K, status,
+  kernel<<<grid, SL_THREADS, R::DYN, stream>>>(A, tiles, scales, out, M, N, K, status,
                                                wait_limit_ns);
   return cudaGetLastError();
+}
+
+template <int MT, int GROUP>
+cudaError_t launch_slices_bs(const __half* A, const uint8_t* tiles, const __half* scales,
+                             const Outputs& out, int M, int N, int K, int grid, int* status,
+                             unsigned long long wait_limit_ns, cudaStream_t stream) {
+  const int slices = N / SLICE_COLS;
+  const int most = (slices + grid - 1) / grid;  // slices of the longest run
+  switch (slice_bs(most)) {
+    case 16:
+      return launch_slices_typed<MT, GROUP, 16>(A, tiles, scales, out, M, N, K, grid, status,
+                                                wait_limit_ns, stream);
+    case 8:
+      return launch_slices_typed<MT, GROUP, 8>(A, tiles, scales, out, M, N, K, grid, status,
+                                               wait_limit_ns, stream);
+    default:
+      return launch_slices_typed<MT, GROUP, 4>(A, tiles, scales, out, M, N, K, grid, status,
+                                               wait_limit_ns, stream);
+  }
 }
 
 int slice_grid(int N, int sm_count) {
@@ -1185,26 +1181,24 @@ bool supported(int M, int K, int group) {
 
 int pick_schedule(int M, int N, int K, int sm_count, size_t workspace_bytes) {
   const int mode = schedule_mode();
-  if ((mode == kScheduleAuto || mode == kScheduleSlices) && slice_grid(N, sm_count) > 0)
-    return kScheduleSlices;
+  if (mode == kScheduleSlices && slice_grid(N, sm_count) > 0) return kScheduleSlices;
   const SkPlan sk = sk_plan(M, N, K, sm_count);
   if (workspace_bytes > 0 && sk.preferred && workspace_bytes >= sk.workspace_bytes)
     return kScheduleStreamK;
   return kScheduleCluster;
 }
 
-cudaError_t launch(const CUtensorMap& act_map, const SliceMaps* maps, const uint8_t* tiles,
+cudaError_t launch(const CUtensorMap& act_map, const __half* A, const uint8_t* tiles,
                    const __half* scales, const Outputs& out, int M, int N, int K, int group,
                    int sm_count, void* workspace, size_t workspace_bytes, int* status,
                    unsigned long long wait_limit_ns, cudaStream_t stream) {
   const int sched = pick_schedule(M, N, K, sm_count, workspace ? workspace_bytes : 0);
   if (sched == kScheduleSlices) {
-    if (!maps) return cudaErrorInvalidValue;
     const int grid = slice_grid(N, sm_count);
 #define I4G_SL_CASE(MT, G)                                                                   \
   if (group == G)                                                                            \
-    return launch_slices_typed<MT, G>(act_map, *maps, scales, out, M, N, K, grid, status,    \
-                                      wait_limit_ns, stream);
+    return launch_slices_bs<MT, G>(A, tiles, scales, out, M, N, K, grid, status,             \
+                                   wait_limit_ns, stream);
     if (M <= 8) {
       I4G_SL_CASE(1, 32) I4G_SL_CASE(1, 64) I4G_SL_CASE(1, 128)
     } else {

@@ -122,19 +122,15 @@ constexpr int kScheduleAuto = 0, kScheduleCluster = 1, kScheduleStreamK = 2, kSc
 // across CTAs). Possible when every CTA owns at most kSliceMax slices.
 constexpr int kSliceMax = 8;
 int slice_grid(int N, int sm_count);  // 0: not possible
-// Weight tensor maps of the slice schedule: box[n-1] loads n slices x 2
-// halves x 4 blocks of one tile ({256 B, 8 slices, 2 halves, K/64, N/128}).
-struct SliceMaps {
-  CUtensorMap box[kSliceMax];
-};
 // The schedule launch() runs for this shape (given a workspace of
 // workspace_bytes), under the current set_schedule choice.
 int pick_schedule(int M, int N, int K, int sm_count, size_t workspace_bytes);
 void set_schedule(int mode);
 // Launches the stream-K schedule when `workspace` holds sk_plan's bytes and
 // it is preferred, else the cluster schedule (no workspace).
-// `maps` is needed for the slice schedule only (else it may be null).
-cudaError_t launch(const CUtensorMap& act_map, const SliceMaps* maps, const uint8_t* tiles,
+// A: the activation rows (read directly by the slice schedule; the others
+// read them through act_map).
+cudaError_t launch(const CUtensorMap& act_map, const __half* A, const uint8_t* tiles,
                    const __half* scales, const Outputs& out, int M, int N, int K, int group,
                    int sm_count, void* workspace, size_t workspace_bytes, int* status,
                    unsigned long long wait_limit_ns, cudaStream_t stream);

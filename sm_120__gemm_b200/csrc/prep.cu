@@ -8,6 +8,7 @@
 // rounding ties. (The reference's own GPU quantiser, src/quantize.cu:22,36,
 // is built with --use_fast_math and so may differ from quantize_cpu there.)
 #include "gemm_tc.h"
+#include "ptx.cuh"
 
 #include <climits>
 #include <cuda_runtime.h>
@@ -356,9 +357,10 @@ __global__ void __launch_bounds__(THREADS)
     const __half s0 = __float2half_rn(max_like_std(__fdiv_rn(vmax.x, 7.0f), 1.0e-8f));
     const __half s1 = __float2half_rn(max_like_std(__fdiv_rn(vmax.y, 7.0f), 1.0e-8f));
     if (part == 0) {
-      *reinterpret_cast<__half2*>(
-          &rscales[(static_cast<size_t>(nt) * groups + kc * GPC + gl) * 128 + 2 * np]) =
-          __halves2half2(s0, s1);
+      // two 2-byte stores: the scale buffer need only be 2-byte aligned
+      __half* sdst = rscales + (static_cast<size_t>(nt) * groups + kc * GPC + gl) * 128 + 2 * np;
+      sdst[0] = s0;
+      sdst[1] = s1;
       const float f0 = __half2float(s0), f1 = __half2float(s1);
       const float kNaN = __int_as_float(0x7fffffff);
       sf[gl][2 * np] = f0;
@@ -410,7 +412,8 @@ cudaError_t quantize_repack(const __half* b, uint8_t* tiles, __half* rscales, in
   switch (group) {
     case 32: quantize_repack_kernel<32><<<grid, THREADS, 0, stream>>>(b, t, rscales, K, N); break;
     case 64: quantize_repack_kernel<64><<<grid, THREADS, 0, stream>>>(b, t, rscales, K, N); break;
-    default: quantize_repack_kernel<128><<<grid, THREADS, 0, stream>>>(b, t, rscales, K, N); break;
+    case 128: quantize_repack_kernel<128><<<grid, THREADS, 0, stream>>>(b, t, rscales, K, N); break;
+    default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
 }

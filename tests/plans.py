@@ -113,11 +113,11 @@ def decode_slice_grid(N, sms):
 def expected_decode_schedule(M, N, K, budget, sms=None, schedule="auto"):
     """(schedule, param, workspace bytes) of a decode launch given `budget`
     bytes of workspace, as i4g_plan reports it: the slice schedule where
-    possible (auto or forced), else stream-K when preferred and the workspace
-    holds it, else the cluster schedule."""
+    forced and possible, else stream-K when preferred and the workspace holds
+    it, else the cluster schedule."""
     sms = sms or sm_count()
     grid = decode_slice_grid(N, sms)
-    if schedule in ("auto", "slices") and grid:
+    if schedule == "slices" and grid:
         return "slices", grid, 0
     pref, sk_grid, need = expected_decode_plan(M, N, K, sms=sms, schedule=schedule)
     if budget > 0 and pref and budget >= need:
