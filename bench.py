@@ -73,19 +73,52 @@ def load_profile_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled during the timed
+    region: NVML read every 2 ms from a thread (read-only queries), or
+    nvidia-smi -lms 20 where NVML cannot be loaded."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
-    def __init__(self, device_index: int):
+    def __init__(self, device_index: int, period_s: float = 0.002):
         self.device_index = device_index
+        self.period_s = period_s
         self.proc = None
+        self.nvml = None
         self.lines = []
+        self.samples = []  # (sm_mhz, max_mhz, reasons) from NVML
         self.first = 0
+        self.stop = threading.Event()
+
+    def _nvml_poll(self):
+        n = self.nvml
+        h = n.nvmlDeviceGetHandleByIndex(self.device_index)
+        mx = n.nvmlDeviceGetMaxClockInfo(h, n.NVML_CLOCK_SM)
+        bits = {"hw_slowdown": n.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": n.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": n.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": n.nvmlClocksEventReasonSwPowerCap}
+        while not self.stop.is_set():
+            try:
+                sm = n.nvmlDeviceGetClockInfo(h, n.NVML_CLOCK_SM)
+                r = n.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((sm, mx, {k for k, b in bits.items() if r & b}))
+            except Exception:  # noqa: BLE001 - a failed read only loses a sample
+                pass
+            self.stop.wait(self.period_s)
 
     def __enter__(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.thread = threading.Thread(target=self._nvml_poll, daemon=True)
+            self.thread.start()
+            return self
+        except Exception:  # noqa: BLE001 - fall back to nvidia-smi
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.QUERY}",
@@ -106,6 +139,13 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        if self.nvml is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
+            try:
+                self.nvml.nvmlShutdown()
+            except Exception:  # noqa: BLE001
+                pass
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -116,23 +156,31 @@ class ClockSampler:
 
     def summary(self):
         sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines[max(0, self.first - 1):]:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower() == "active":
-                    reasons.add(name)
+        if self.nvml is not None:
+            for s_mhz, m_mhz, rs in self.samples:
+                sm.append(float(s_mhz))
+                mx = float(m_mhz)
+                reasons |= rs
+            source = f"NVML every {self.period_s * 1e3:.0f} ms"
+        else:
+            for line in self.lines[max(0, self.first - 1):]:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx = float(parts[2])
+                except ValueError:
+                    continue
+                for name, val in zip(self.NAMES, parts[5:9]):
+                    if val.lower() == "active":
+                        reasons.add(name)
+            source = "nvidia-smi -lms 20"
         if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0,
+                    "source": source}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": source}
 
 
 # ------------------------------------------------------------ our arm
