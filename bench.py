@@ -661,6 +661,95 @@ def cpu_baseline(args, sample_rows):
                               "seconds_measured": round(t_deq1 + t_rows1, 3)}}
 
 
+def _reference_gpu_worker(q, iters):
+    """Child process: the reference's final GPU kernel at the headline shape,
+    per group, with rotating inputs as in run_ours (reference layouts made by
+    this library's byte-exact quantize and repacks, outside the timing)."""
+    import torch
+
+    import oracle
+    import sm_120__gemm_b200 as i4g
+
+    R = oracle.ref_final_kernel()
+    if R is None:
+        q.put({"unavailable": "oracle/_ref/libi4g_reffinal.so not loadable"})
+        return
+    M, N, K = M_HEAD, N_HEAD, K_HEAD
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(1234)
+    acts = [(torch.rand(M, K, generator=gen, device=dev) * 2 - 1).half() for _ in range(4)]
+    c = torch.empty(M, N, dtype=torch.float16, device=dev)
+    stream = torch.cuda.current_stream()
+    out = {}
+    for g in GROUPS:
+        sets = []
+        for r in range(2):
+            w = (torch.randn(K, N, generator=gen, device=dev) * 0.02).half()
+            packed = torch.empty(K * N // 2, dtype=torch.uint8, device=dev)
+            scales = torch.empty(K // g, N, dtype=torch.float16, device=dev)
+            i4g.launch_quantize(w, packed, scales, K, N, g)
+            b = torch.empty_like(packed)
+            (i4g.launch_repack_mma_128x32 if g == 64 else i4g.launch_repack_mma_pair_128x32)(
+                packed, b, K, N)
+            s = torch.empty_like(scales)
+            i4g.launch_repack_scales_128(scales, s, K, N, g)
+            sets.append((b, s))
+
+        def call(i):
+            b, s = sets[i % 2]
+            return R.i4r_launch_final(acts[(3 * i + 1) % 4].data_ptr(), b.data_ptr(), s.data_ptr(),
+                                      c.data_ptr(), M, N, K, g, stream.cuda_stream)
+        for i in range(3):
+            if call(i) != 0:
+                q.put({"unavailable": f"reference launch failed (group {g})"})
+                return
+        torch.cuda.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(iters)]
+        for i, (e0, e1) in enumerate(ev):
+            e0.record(stream)
+            call(i)
+            e1.record(stream)
+        torch.cuda.synchronize()
+        ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev)
+        out[str(g)] = {"kernel_ms": round(ms, 4), "tflops": round(flops(M, N, K) / ms / 1e9, 1)}
+    total = sum(v["kernel_ms"] for v in out.values())
+    q.put({"per_group": out, "tflops": round(len(GROUPS) * flops(M, N, K) / total / 1e9, 1)})
+
+
+def reference_gpu_row(iters=20, limit_s=240):
+    """Context row (not the arm's value): the reference's own final GPU GEMM
+    (kernels/gemm_final.cu:5-13 over kernels/gemm_v17_instruction.cu,
+    compiled unmodified for sm_100a by oracle/Makefile) on this box, at the
+    headline workload. Its waits are unbounded, so it runs in a child process
+    stopped after `limit_s`."""
+    import multiprocessing as mp
+
+    import torch
+    if not torch.cuda.is_available():
+        return {"unavailable": "no GPU"}
+    if not os.path.exists(os.path.join(ROOT, "oracle", "_ref", "libi4g_reffinal.so")):
+        return {"unavailable": "oracle/_ref/libi4g_reffinal.so not built (needs the reference)"}
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_reference_gpu_worker, args=(q, iters))
+    p.start()
+    p.join(limit_s)
+    if p.is_alive():
+        p.kill()
+        p.join()
+        return {"unavailable": f"did not finish within {limit_s} s"}
+    if p.exitcode != 0:
+        return {"unavailable": f"child exited with {p.exitcode}"}
+    row = q.get(timeout=10)
+    row["kernel"] = ("the reference's final kernel (V18a g32 / V17b g64 / V18b g128, "
+                     "mma.sync + TMA), built for sm_100a from its own source")
+    row["inputs"] = ("reference layouts (mma pair / mma fragments, 128-column scales) from "
+                     "this library's byte-exact quantize and repacks, outside the timing; "
+                     "rotating inputs as in the main arm")
+    return row
+
+
 def run_reference(args):
     """Each step times the reference's CPU path on one bounded sample (one
     group per step, cycling 32/64/128: the full dequantize_cpu plus
@@ -693,6 +782,7 @@ def run_reference(args):
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
+        "reference_gpu_kernel": reference_gpu_row() if not args.no_extras else None,
     }
 
 

@@ -131,7 +131,9 @@ def ref_lib():
 
 
 _REFQ_LIB = os.path.join(HERE, "_ref", "libi4g_refquant.so")
+_REFF_LIB = os.path.join(HERE, "_ref", "libi4g_reffinal.so")
 _refq = None
+_reff = None
 
 
 def ref_gpu_quantizer():
@@ -147,6 +149,26 @@ def ref_gpu_quantizer():
             R.i4r_gpu_quantize.restype = _i
             _refq = R
     return _refq
+
+
+def ref_final_kernel():
+    """The reference's own final GPU GEMM (kernels/gemm_final.cu:5-13 over
+    kernels/gemm_v17_instruction.cu, built for sm_100a), as
+    i4r_launch_final(a, b, scales, c, M, N, K, group, stream) on device
+    pointers in the reference's layouts; None when it was not built or no
+    CUDA driver is present. Its
+    waits are unbounded: run it under a host timeout."""
+    global _reff
+    with _lock:
+        if _reff is None and os.path.exists(_REFF_LIB):
+            try:
+                R = ctypes.CDLL(_REFF_LIB)
+            except OSError:  # no CUDA driver here (a CPU-only machine)
+                return None
+            R.i4r_launch_final.argtypes = [ctypes.c_void_p] * 4 + [_i] * 4 + [ctypes.c_void_p]
+            R.i4r_launch_final.restype = _i
+            _reff = R
+    return _reff
 
 
 def _p(arr, ptype):
