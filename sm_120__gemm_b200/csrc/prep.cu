@@ -379,9 +379,12 @@ __global__ void __launch_bounds__(THREADS)
     const int h = rr >> 8, np = (rr >> 2) & 63, w = rr & 3;
     const int kk0 = jb * 64 + h * 32 + w * 8;  // row inside the slab
     const int gl = kk0 / GROUP;
+    // the 8 rows kk0 .. kk0 + 7 share one chunk swizzle: one base address,
+    // then a row stride of 128 halves
+    const __half2* xp = reinterpret_cast<const __half2*>(&slab[chunk_at(kk0, np >> 2) + 2 * (np & 3)]);
     __half2 x[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) x[e] = pair_at(kk0 + e, np);
+    for (int e = 0; e < 8; ++e) x[e] = xp[e * 64];
     uint32_t lo, hi;
     // a NaN reciprocal (scale not a finite normal number) makes every d NaN
     if (!codes8(x, make_float2(sr[gl][2 * np], sr[gl][2 * np + 1]), lo, hi)) {
