@@ -310,10 +310,15 @@ __device__ __forceinline__ bool codes8(const __half2 (&x)[8], float2 r, uint32_t
 // The slab sits in shared memory as rows of sixteen 16-byte chunks, chunk c
 // of row k stored at c ^ (2 ((k / 8) % 4)): the code pass reads rows k, k+8,
 // k+16, k+24 at once, which this spreads over all 32 banks.
-template <int GROUP>
+//
+// ROWMAJOR = true writes the reference's formats instead (quantize_cpu's
+// packed bytes, row-major scales [K / g][N]); its code pass maps a warp to 32
+// consecutive column pairs of the same 8 rows, so each row's 32 code bytes
+// are one store.
+template <int GROUP, bool ROWMAJOR>
 __global__ void __launch_bounds__(THREADS)
-    quantize_repack_kernel(const __half* __restrict__ b, uint32_t* __restrict__ tiles,
-                           __half* __restrict__ rscales, int K, int N) {
+    quantize_repack_kernel(const __half* __restrict__ b, void* __restrict__ codes,
+                           __half* __restrict__ scales_out, int K, int N) {
   constexpr int KC = GROUP > 64 ? GROUP : 64;
   constexpr int GPC = KC / GROUP;           // groups per slab
   constexpr int P = THREADS / (64 * GPC);   // threads per (group, column pair)
@@ -358,7 +363,9 @@ __global__ void __launch_bounds__(THREADS)
     const __half s1 = __float2half_rn(max_like_std(__fdiv_rn(vmax.y, 7.0f), 1.0e-8f));
     if (part == 0) {
       // two 2-byte stores: the scale buffer need only be 2-byte aligned
-      __half* sdst = rscales + (static_cast<size_t>(nt) * groups + kc * GPC + gl) * 128 + 2 * np;
+      __half* sdst =
+          ROWMAJOR ? scales_out + static_cast<size_t>(kc * GPC + gl) * N + nt * 128 + 2 * np
+                   : scales_out + (static_cast<size_t>(nt) * groups + kc * GPC + gl) * 128 + 2 * np;
       sdst[0] = s0;
       sdst[1] = s1;
       const float f0 = __half2float(s0), f1 = __half2float(s1);
@@ -376,12 +383,15 @@ __global__ void __launch_bounds__(THREADS)
 #pragma unroll 1
   for (int i = threadIdx.x; i < (KC / 64) * 512; i += THREADS) {
     const int jb = i >> 9, rr = i & 511;
-    const int h = rr >> 8, np = (rr >> 2) & 63, w = rr & 3;
+    const int h = rr >> 8;
+    const int np = ROWMAJOR ? (rr & 63) : ((rr >> 2) & 63);
+    const int w = ROWMAJOR ? ((rr >> 6) & 3) : (rr & 3);
     const int kk0 = jb * 64 + h * 32 + w * 8;  // row inside the slab
     const int gl = kk0 / GROUP;
     // the 8 rows kk0 .. kk0 + 7 share one chunk swizzle: one base address,
     // then a row stride of 128 halves
-    const __half2* xp = reinterpret_cast<const __half2*>(&slab[chunk_at(kk0, np >> 2) + 2 * (np & 3)]);
+    const __half2* xp =
+        reinterpret_cast<const __half2*>(&slab[chunk_at(kk0, np >> 2) + 2 * (np & 3)]);
     __half2 x[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) x[e] = xp[e * 64];
@@ -398,24 +408,42 @@ __global__ void __launch_bounds__(THREADS)
         hi |= static_cast<uint32_t>(quantize_one(v.y, f1) & 15) << sh;
       }
     }
-    uint32_t* dst = tiles + (static_cast<size_t>(nt) * kblocks + kc * (KC / 64) + jb) * 1024 +
-                    h * 512 + (2 * np) * 4 + w;
-    dst[0] = lo;
-    dst[4] = hi;
+    if constexpr (ROWMAJOR) {
+      // row k0 + kk0 + e: byte (column pair nt * 64 + np) = lo code | hi code << 4
+      uint8_t* dst = static_cast<uint8_t*>(codes) + static_cast<size_t>(k0 + kk0) * (N / 2) +
+                     nt * 64 + np;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int sh = 4 * (e >> 1) + 16 * (e & 1);
+        dst[static_cast<size_t>(e) * (N / 2)] =
+            static_cast<uint8_t>(((lo >> sh) & 15u) | (((hi >> sh) & 15u) << 4));
+      }
+    } else {
+      uint32_t* dst = static_cast<uint32_t*>(codes) +
+                      (static_cast<size_t>(nt) * kblocks + kc * (KC / 64) + jb) * 1024 + h * 512 +
+                      (2 * np) * 4 + w;
+      dst[0] = lo;
+      dst[4] = hi;
+    }
   }
+}
+
+template <int GROUP, bool ROWMAJOR>
+void launch_slab(dim3 grid, const __half* b, void* codes, __half* scales, int K, int N,
+                 cudaStream_t stream) {
+  quantize_repack_kernel<GROUP, ROWMAJOR><<<grid, THREADS, 0, stream>>>(b, codes, scales, K, N);
 }
 
 }  // namespace
 
 cudaError_t quantize_repack(const __half* b, uint8_t* tiles, __half* rscales, int K, int N,
                             int group, cudaStream_t stream) {
-  uint32_t* t = reinterpret_cast<uint32_t*>(tiles);
   const int kc = group > 64 ? group : 64;
   const dim3 grid(N / 128, K / kc);
   switch (group) {
-    case 32: quantize_repack_kernel<32><<<grid, THREADS, 0, stream>>>(b, t, rscales, K, N); break;
-    case 64: quantize_repack_kernel<64><<<grid, THREADS, 0, stream>>>(b, t, rscales, K, N); break;
-    case 128: quantize_repack_kernel<128><<<grid, THREADS, 0, stream>>>(b, t, rscales, K, N); break;
+    case 32: launch_slab<32, false>(grid, b, tiles, rscales, K, N, stream); break;
+    case 64: launch_slab<64, false>(grid, b, tiles, rscales, K, N, stream); break;
+    case 128: launch_slab<128, false>(grid, b, tiles, rscales, K, N, stream); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
@@ -423,6 +451,19 @@ cudaError_t quantize_repack(const __half* b, uint8_t* tiles, __half* rscales, in
 
 cudaError_t quantize(const __half* b, uint8_t* packed, __half* scales, int K, int N, int group,
                      cudaStream_t stream) {
+  // whole slabs (and a 16-byte aligned B): one pass, B read once
+  const int kc = group > 64 ? group : 64;
+  if ((group == 32 || group == 64 || group == 128) && N % 128 == 0 && K >= kc && K % kc == 0 &&
+      reinterpret_cast<uintptr_t>(b) % 16 == 0) {
+    const dim3 grid(N / 128, K / kc);
+    switch (group) {
+      case 32: launch_slab<32, true>(grid, b, packed, scales, K, N, stream); break;
+      case 64: launch_slab<64, true>(grid, b, packed, scales, K, N, stream); break;
+      default: launch_slab<128, true>(grid, b, packed, scales, K, N, stream); break;
+    }
+    return cudaGetLastError();
+  }
+  // any other shape (partial groups, odd widths): one thread per column pair and group
   const int groups = (K + group - 1) / group;
   const int pairs = N / 2;
   const dim3 grid((pairs + 127) / 128, groups);
