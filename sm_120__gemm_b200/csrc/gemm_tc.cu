@@ -327,18 +327,16 @@ __device__ __forceinline__ void shift_down4(uint32_t (&hb)[NW]) {
 
 // Whole-tile epilogue with several copies of C (this GPU's and peers'), for
 // one thread's slice (TMEM lane `row`, COLS accumulator columns from col0):
-// the slice is read, converted and the accumulator released as in the plain
-// path, then stored into this GPU's copy (dst[0]). Once every epilogue thread
-// has stored its slice (GPU-scope fence, then the epilogue barrier) the
-// finished tile is read back from L2 and copied to the peers' copies in
-// 16-byte pieces, so the NVLink traffic moves in full 16-byte stores and the
-// next tile's MMAs never wait on it. Every epilogue thread takes the barrier
-// whatever `ok` is (a failed wait skips the work, never the barrier).
+// the slice is read, converted and stored into this GPU's copy (dst[0]), the
+// accumulator released once the last chunk is in registers. Then a GPU-scope
+// fence and the epilogue barrier (which every epilogue thread takes whatever
+// `ok` is: a failed wait skips the work, never the barrier); true when every
+// thread's slice is stored. The tile then goes to the peers' copies piece by
+// piece while the epilogue waits for later accumulators (PeerCopier).
 template <int TILE_M, int CG>
-__device__ __forceinline__ void copies_epilogue(bool ok, const Outputs& out, int M, int mt, int nt,
-                                             int half, int row, int m0, uint32_t col0,
-                                             const uint32_t* hb, uint32_t empty_bar, int epi_warp,
-                                             int lane) {
+__device__ __forceinline__ bool copies_epilogue(bool ok, const Outputs& out, int M, int mt, int nt,
+                                                int half, int row, int m0, uint32_t col0,
+                                                const uint32_t* hb, uint32_t empty_bar) {
   constexpr int COLS = TILE_M / 4;
   constexpr int EPI_THREADS = NUM_EPI_WARPS * 32;
   const size_t ldc = static_cast<size_t>(out.ldc);
@@ -366,22 +364,59 @@ __device__ __forceinline__ void copies_epilogue(bool ok, const Outputs& out, int
       }
     }
   }
-  if (out.count == 1) return;
   __threadfence();
-  if (!epi_bar_and(EPI_THREADS, ok)) return;
-  const int rows = min(TILE_M, M - mt * TILE_M);
-  // 16 pieces of 16 bytes per 128-column row; consecutive threads take
-  // consecutive pieces of a row
-#pragma unroll 1
-  for (int piece = epi_warp * 32 + lane; piece < rows * 16; piece += EPI_THREADS) {
-    const size_t off = static_cast<size_t>(piece >> 4) * ldc + (piece & 15) * 8;
-    const uint4 v = __ldcg(reinterpret_cast<const uint4*>(tile0 + off));
-#pragma unroll 1
-    for (int d = 1; d < out.count; ++d)
-      *reinterpret_cast<uint4*>(static_cast<__half*>(out.dst[d]) + tile_off + off) = v;
-  }
-  __threadfence_system();  // peer copies are read by other GPUs
+  return epi_bar_and(EPI_THREADS, ok);
 }
+
+// One epilogue thread's share of copying finished whole tiles from this
+// GPU's copy of C to the peers' copies: pieces t, t + 512, ... of each tile
+// (16 bytes each, 16 per 128-column row), read back from L2 (the tile's
+// local stores were fenced before the epilogue barrier that made it
+// `ready`). Tiles are this CTA's items in order; `ready` counts the items
+// the epilogue has finished (split items, which the reduction writes to
+// every copy itself, are skipped). Each thread walks its own pieces, so no
+// barrier is needed between pieces, and the copying fills the time the
+// epilogue would otherwise spend waiting for the next accumulator.
+template <int TILE_M, int CG>
+struct PeerCopier {
+  const Outputs* out;
+  int M, first;        // rows of C; this thread's first piece
+  int next = 0;        // item being copied
+  int ready = 0;       // items finished by the epilogue
+  int piece = 0;       // this thread's next piece of item `next`
+  int rows = -1;       // rows of item `next` (-1: not looked up yet; 0: nothing to copy)
+  size_t tile_off = 0;
+
+  __device__ __forceinline__ bool pending() const { return next < ready; }
+
+  // Copies up to `budget` pieces; `item(j, w)` looks up this CTA's item j.
+  template <typename ItemFn>
+  __device__ __forceinline__ void copy(int budget, ItemFn item, int rank) {
+    const size_t ldc = static_cast<size_t>(out->ldc);
+    while (budget > 0 && next < ready) {
+      if (rows < 0) {
+        Item w;
+        item(next, w);
+        const int nt = w.nt * CG + rank;
+        rows = w.rem < 0 ? min(TILE_M, M - w.mt * TILE_M) : 0;
+        tile_off = static_cast<size_t>(w.mt * TILE_M) * ldc + out->col0 + nt * TILE_N;
+        piece = first;
+      }
+      if (piece >= rows * 16) {
+        ++next;
+        rows = -1;
+        continue;
+      }
+      const size_t off = tile_off + static_cast<size_t>(piece >> 4) * ldc + (piece & 15) * 8;
+      const uint4 v = __ldcg(reinterpret_cast<const uint4*>(static_cast<__half*>(out->dst[0]) + off));
+#pragma unroll 1
+      for (int d = 1; d < out->count; ++d)
+        *reinterpret_cast<uint4*>(static_cast<__half*>(out->dst[d]) + off) = v;
+      piece += NUM_EPI_WARPS * 32;
+      --budget;
+    }
+  }
+};
 
 // Rotates a running-sum array down by two words (the first two move to the
 // end), so that a rolled loop over 8-column chunks always updates words 0, 1
@@ -735,7 +770,20 @@ __global__ void __launch_bounds__(THREADS, 1)
       if constexpr (PAIR) mbar_arrive_cluster_relaxed(lead(dempty(acc)));
       else mbar_arrive(dempty(acc));
     };
+    auto item_at = [&](int jj, Item& wi) {
+      next_item(sched, unit, units, jj, kblocks, num_m, num_n, wi);
+    };
+    PeerCopier<TILE_M, CG> copier{&out, M, (warp - FIRST_EPI_WARP) * 32 + lane};
     auto wait_full = [&](int acc, uint32_t parity) {
+      if constexpr (MULTI) {
+        // finished tiles go to the peers while this accumulator fills
+        while (copier.pending()) {
+          if (PAIR ? mbar_test_cluster(dfull(acc), parity) : mbar_test(dfull(acc), parity))
+            return true;
+          if (*abort_flag) return false;
+          copier.copy(2, item_at, static_cast<int>(rank));
+        }
+      }
       return PAIR ? mbar_wait_cluster(dfull(acc), parity, abort_flag, status, wait_limit_ns)
                   : mbar_wait(dfull(acc), parity, abort_flag, status, wait_limit_ns);
     };
@@ -777,9 +825,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (w.rem < 0) {
         // ------------------------------------------------ whole tile -> C
         if constexpr (MULTI) {
-          copies_epilogue<TILE_M, CG>(ok, out, M, w.mt, nt, half, row, m0, col0, hb,
-                                      lead(dempty(acc)), warp - FIRST_EPI_WARP, lane);
+          const bool all = copies_epilogue<TILE_M, CG>(ok, out, M, w.mt, nt, half, row, m0, col0,
+                                                       hb, lead(dempty(acc)));
           if (!ok) failed = true;
+          if (all) copier.ready = j + 1;
           continue;
         }
         if (!ok) {
@@ -881,6 +930,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       epi_bar_sync(EPI_THREADS);  // the ticket slot is read by all before it changes
       if (last && warp == FIRST_EPI_WARP && lane == 0) tickets[ticket] = 0u;
+      if constexpr (MULTI) copier.ready = j + 1;  // (split items are not copied)
+    }
+    if constexpr (MULTI) {
+      // the rest of the copies, then make every peer store visible to the
+      // other GPUs before the kernel ends
+      if (!failed) copier.copy(INT_MAX, item_at, static_cast<int>(rank));
+      __threadfence_system();
     }
   }
 
