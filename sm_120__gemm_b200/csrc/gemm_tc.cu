@@ -82,7 +82,7 @@ constexpr int ACC_COL0 = T_STAGES * T_COLS;    // 256
 constexpr int WBLOCK_BYTES = TILE_N * BK / 2;  // 4096: one tile-layout block
 constexpr int SCALE_BYTES = 512;               // up to two groups x 128 halves
 constexpr int W_SLOT = WBLOCK_BYTES + SCALE_BYTES;
-constexpr int W_STAGES = 8;
+constexpr int W_STAGES = 14;
 constexpr int GROUP_M = 8;                     // rasterisation band (m-tiles)
 
 // CG = 1: one CTA per tile. CG = 2: a CTA pair (cluster of two) per tile of
@@ -284,14 +284,15 @@ __device__ __forceinline__ void high_parts(uint32_t w, float (&h)[4]) {
   h[3] = b.y;
 }
 
-// Promotes 8 accumulator columns at taddr (hb words 0, 1): S = H + D (one
-// FP32 rounding per value), H <- e5m2(S), D <- S - H (exact), stored back.
-__device__ __forceinline__ void promote_chunk(uint32_t taddr, uint32_t* hb) {
-  uint32_t v[8];
-  tmem_ld_32x32b_x8(taddr, v);
-  tmem_ld_wait8(v);
+// Promotes 16 accumulator columns at taddr (hb words 0..3), read with one
+// load wait: S = H + D (one FP32 rounding per value), H <- e5m2(S),
+// D <- S - H (exact), stored back.
+__device__ __forceinline__ void promote_chunk16(uint32_t taddr, uint32_t* hb) {
+  uint32_t v[16];
+  tmem_ld_32x32b_x16(taddr, v);
+  tmem_ld_wait16(v);
 #pragma unroll
-  for (int q = 0; q < 2; ++q) {
+  for (int q = 0; q < 4; ++q) {
     float h[4], sum[4];
     high_parts(hb[q], h);
 #pragma unroll
@@ -301,7 +302,14 @@ __device__ __forceinline__ void promote_chunk(uint32_t taddr, uint32_t* hb) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) v[4 * q + i] = __float_as_uint(sum[i] - h[i]);
   }
-  tmem_st_32x32b_x8(taddr, v);
+  uint32_t a[8], b[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    a[i] = v[i];
+    b[i] = v[8 + i];
+  }
+  tmem_st_32x32b_x8(taddr, a);
+  tmem_st_32x32b_x8(taddr + 8, b);
 }
 
 // Final read of 16 accumulator columns (hb words 0..3): v = H + D in FP32.
@@ -805,8 +813,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (ok) {
           tc_fence_after();
 #pragma unroll 1
-          for (int c = 0; c < COLS / 8; ++c) {
-            promote_chunk(col0 + c * 8, hb);
+          for (int c = 0; c < COLS / 16; ++c) {
+            promote_chunk16(col0 + c * 16, hb);
+            rotate_down2(hb);
             rotate_down2(hb);
           }
           tmem_st_wait();
@@ -858,19 +867,23 @@ __global__ void __launch_bounds__(THREADS, 1)
           // is released once the last chunk is in registers
           __half* cp = static_cast<__half*>(out.dst[0]) + static_cast<size_t>(m0) * N + n;
           const int valid = min(COLS, M - m0);
+          // the whole slice is read and rounded to FP16 pairs before the
+          // accumulator is released; the stores follow
+          __half2 hv[COLS / 2];
 #pragma unroll
           for (int c = 0; c < COLS / 16; ++c) {
             uint32_t v[16];
             load_sum16(col0 + c * 16, &hb[c * 4], v);
-            if (c == COLS / 16 - 1) {
-              tc_fence_before();
-              release(acc);
-            }
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              if (c * 16 + j < valid) *cp = __float2half_rn(__uint_as_float(v[j]));
-              cp += N;
-            }
+            for (int j = 0; j < 8; ++j)
+              hv[c * 8 + j] = __floats2half2_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+          }
+          tc_fence_before();
+          release(acc);
+#pragma unroll
+          for (int j = 0; j < COLS; ++j) {
+            if (j < valid) *cp = (j & 1) ? __high2half(hv[j >> 1]) : __low2half(hv[j >> 1]);
+            cp += N;
           }
         }
         continue;
