@@ -85,25 +85,35 @@ constexpr int W_SLOT = WBLOCK_BYTES + SCALE_BYTES;
 constexpr int W_STAGES = 14;
 constexpr int GROUP_M = 8;                     // rasterisation band (m-tiles)
 
-// CG = 1: one CTA per tile. CG = 2: a CTA pair (cluster of two) per tile of
-// 2 x 128 weight columns, each CTA loading half of the TILE_M activation rows.
+// CG = 1: one CTA per tile, weights dequantised into TMEM (operand A from
+// TMEM). CG = 2: a CTA pair (cluster of two) per tile of 2 x 128 weight
+// columns, each CTA loading half of the TILE_M activation rows and
+// dequantising its 128 weight columns into 128B-swizzled shared memory (both
+// operands from shared memory), so that all of TMEM holds two accumulators.
 template <int TILE_M, int CG>
 struct Cfg {
-  static constexpr int ACC = TILE_M <= 128 ? 2 : 1;  // accumulators in TMEM
-  static constexpr int ROWS = TILE_M / CG;           // activation rows this CTA loads
+  static constexpr bool SS = CG == 2;                          // weights in smem
+  static constexpr int ACC = (SS || TILE_M <= 128) ? 2 : 1;    // accumulators in TMEM
+  static constexpr int ACC_COL = SS ? 0 : ACC_COL0;            // first accumulator column
+  static constexpr int ROWS = TILE_M / CG;                     // activation rows this CTA loads
   static constexpr int ACT_BYTES = ROWS * BK * 2;
-  static constexpr int A_STAGES = (CG == 2 || TILE_M <= 128) ? 8 : 5;
+  static constexpr int A_STAGES = SS ? 6 : (TILE_M <= 128 ? 8 : 5);
+  static constexpr int W_ST = SS ? 8 : W_STAGES;               // packed weight stages
+  static constexpr int T_ST = SS ? 4 : T_STAGES;               // dequantised weight stages
+  static constexpr int DEQ_BYTES = TILE_N * BK * 2;            // one smem weight tile (SS)
   static constexpr int ACT_OFF = 0;
-  static constexpr int W_OFF = ACT_OFF + A_STAGES * ACT_BYTES;
-  static constexpr int BAR_OFF = W_OFF + W_STAGES * W_SLOT;
-  static constexpr int NUM_BARS = 2 * A_STAGES + 2 * W_STAGES + 2 * T_STAGES + 2 * ACC + 1;
+  static constexpr int DEQ_OFF = ACT_OFF + A_STAGES * ACT_BYTES;
+  static constexpr int W_OFF = DEQ_OFF + (SS ? T_ST * DEQ_BYTES : 0);
+  static constexpr int BAR_OFF = W_OFF + W_ST * W_SLOT;
+  static constexpr int NUM_BARS = 2 * A_STAGES + 2 * W_ST + 2 * T_ST + 2 * ACC + 1;
   static constexpr int MISC_OFF = BAR_OFF + NUM_BARS * 8;
   static constexpr int TOTAL = MISC_OFF + 16;
   static constexpr int DYN_BYTES = TOTAL + 1024;  // slack for 1024-byte alignment
   static_assert(ACT_BYTES % 1024 == 0, "activation stage must keep 1024B alignment");
-  static_assert(ACC_COL0 + ACC * TILE_M <= TMEM_COLS, "TMEM budget");
+  static_assert(DEQ_BYTES % 1024 == 0, "weight tile must keep 1024B alignment");
+  static_assert(ACC_COL + ACC * TILE_M <= TMEM_COLS, "TMEM budget");
   static_assert(DYN_BYTES <= 232448, "shared memory budget");
-  static_assert(T_STAGES % DEQ_GROUPS == 0 && W_STAGES % DEQ_GROUPS == 0, "stage ownership");
+  static_assert(T_ST % DEQ_GROUPS == 0 && W_ST % DEQ_GROUPS == 0, "stage ownership");
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mt, int& nt) {
@@ -455,6 +465,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   using L = Cfg<TILE_M, CG>;
   constexpr int A_STAGES = L::A_STAGES;
   constexpr int ACC = L::ACC;
+  constexpr int W_STAGES = L::W_ST;
+  constexpr int T_STAGES = L::T_ST;
+  constexpr int ACC_COL0 = L::ACC_COL;
   constexpr bool FP32_OUT = OUT == kOutFloat;
   constexpr bool MULTI = OUT == kOutHalfCopies;
   constexpr bool PAIR = CG == 2;
@@ -464,6 +477,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const uint32_t act_base = smem_u32(smem + L::ACT_OFF);
   const uint32_t w_base = smem_u32(smem + L::W_OFF);
+  const uint32_t deq_base = smem_u32(smem + L::DEQ_OFF);  // pairs: weight tiles
   const uint32_t bar_base = smem_u32(smem + L::BAR_OFF);
   // barrier order: afull, aempty, wfull, wempty, tfull, tempty, dfull, dempty, drain
   auto afull = [&](int i) { return bar_base + 8u * i; };
@@ -520,7 +534,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(wempty(i), 4);  // the four warps of the dequant group that read it
     }
     for (int i = 0; i < T_STAGES; ++i) {
-      mbar_init(tfull(i), CG * 4 * 32);  // the dequant threads of both CTAs of a pair
+      // single CTAs: every dequant thread (TMEM stores); pairs: one arrival
+      // per local dequant warp, and in the even CTA also the odd CTA's relay
+      mbar_init(tfull(i), PAIR ? (leader ? 4 + 1 : 4) : 4 * 32);
       mbar_init(tempty(i), 1);           // MMA completion
     }
     for (int i = 0; i < ACC; ++i) {
@@ -667,13 +683,16 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t b_addr = act_base + s * L::ACT_BYTES;
 #pragma unroll
           for (int k16 = 0; k16 < BK / 16; ++k16) {
-            const uint32_t a_tmem = tmem_base + ts * T_COLS + k16 * 8;
             const uint64_t b_desc = smem_desc_sw128(b_addr + k16 * 32);
             // the item's first MMA starts the sum; later ones (including a
             // segment's first, onto the promoted remainder) accumulate
             const uint32_t accumulate = (kb != w.kb0) || (k16 != 0);
-            if constexpr (PAIR) mma_f16_ts_pair(d_tmem, a_tmem, b_desc, IDESC, accumulate);
-            else mma_f16_ts(d_tmem, a_tmem, b_desc, IDESC, accumulate);
+            if constexpr (PAIR) {
+              const uint64_t a_desc = smem_desc_sw128(deq_base + ts * L::DEQ_BYTES + k16 * 32);
+              mma_f16_ss_pair(d_tmem, a_desc, b_desc, IDESC, accumulate);
+            } else {
+              mma_f16_ts(d_tmem, tmem_base + ts * T_COLS + k16 * 8, b_desc, IDESC, accumulate);
+            }
           }
           commit(aempty(s));
           commit(tempty(ts));
@@ -688,8 +707,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       commit(drain_bar);
     }
     if (PAIR && !leader && lane == 0) {
-      // odd CTA of a pair: its activation half landed -> tell the even CTA,
-      // whose MMAs read it
+      // odd CTA of a pair: its activation half landed, its weight tile is
+      // stored -> tell the even CTA, whose MMAs read them
       uint32_t total = 0;
       Item w;
       for (int j = 0; next_item(sched, unit, units, j, kblocks, num_m, num_n, w); ++j)
@@ -698,6 +717,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int s = it % A_STAGES;
         if (!mbar_wait(afull(s), (it / A_STAGES) & 1u, abort_flag, status, wait_limit_ns)) break;
         mbar_arrive_cluster_relaxed(lead(afull(s)));
+        const int ts = it % T_STAGES;
+        if (!mbar_wait(tfull(ts), (it / T_STAGES) & 1u, abort_flag, status, wait_limit_ns)) break;
+        mbar_arrive_cluster_relaxed(lead(tfull(ts)));
       }
     }
     if (lane == 0) mbar_wait(drain_bar, 0, never, nullptr, 100000000ull);
@@ -718,7 +740,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t ph = (it / W_STAGES) & 1u;
       const int ts = it % T_STAGES;
       const uint32_t tph = (it / T_STAGES) & 1u;
-      if (!mbar_wait(wfull(s), ph, abort_flag, status, wait_limit_ns)) break;
+      {
+        const bool landed = mbar_wait(wfull(s), ph, abort_flag, status, wait_limit_ns);
+        if (!(PAIR ? __all_sync(0xffffffffu, landed) : landed)) break;
+      }
       const uint32_t wsrc = w_base + s * W_SLOT + row * 16;
       uint4 c0, c1;
       asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
@@ -750,13 +775,34 @@ __global__ void __launch_bounds__(THREADS, 1)
       const bool free = PAIR ? mbar_wait_cluster(tempty(ts), tph ^ 1u, abort_flag, status,
                                                  wait_limit_ns)
                              : mbar_wait(tempty(ts), tph ^ 1u, abort_flag, status, wait_limit_ns);
-      if (!free) break;
-      tc_fence_after();
-      tmem_st_32x32b_x32(tmem_base + lane_addr + ts * T_COLS, r);
-      tmem_st_wait();
-      tc_fence_before();
-      if constexpr (PAIR) mbar_arrive_cluster_relaxed(lead(tfull(ts)));
-      else mbar_arrive(tfull(ts));
+      if constexpr (PAIR) {
+        // row `row` (128 bytes, 64 k) of this CTA's 128-row weight tile, in
+        // the 128-byte swizzle the MMA's descriptor expects (16-byte chunk c
+        // of row r at chunk c ^ (r % 8)); then, once every lane's stores are
+        // visible to the tensor core (async proxy), one arrival per warp on
+        // this CTA's barrier (the odd CTA's relay forwards it to the even
+        // CTA). The wait's outcome is made warp-uniform so that no warp
+        // splits across __syncwarp.
+        if (!__all_sync(0xffffffffu, free)) break;
+        const uint32_t tile = deq_base + ts * L::DEQ_BYTES + row * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(
+                           tile + ((c ^ (row & 7)) << 4)),
+                       "r"(r[4 * c]), "r"(r[4 * c + 1]), "r"(r[4 * c + 2]), "r"(r[4 * c + 3])
+                       : "memory");
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tfull(ts));
+      } else {
+        if (!free) break;
+        tc_fence_after();
+        tmem_st_32x32b_x32(tmem_base + lane_addr + ts * T_COLS, r);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(tfull(ts));
+      }
     }
   } else {
     // --------------------------------------------------------------- epilogue
