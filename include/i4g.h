@@ -266,9 +266,10 @@ int i4g_plan(int M, int N, int K, int group, int fp32_out, int sm_count,
 
 /* With the I4G_PAIR=1 environment variable (read at the first launch) the
  * tcgen05 kernel runs 256-row tiles on CTA pairs (thread-block clusters of
- * two, one 2-SM tensor-core instruction per pair) when N % 256 == 0, with
- * whole-tile or equal-split tails (no stream-K); by default it runs single
- * CTAs, which are as fast. i4g_plan assumes sm_count / 2 pairs resident at
+ * two, one 2-SM tensor-core instruction per pair, both operands from
+ * shared memory) when N % 256 == 0, with whole-tile or equal-split tails (no
+ * stream-K); by default it runs single CTAs, which measured slightly faster
+ * on B200. i4g_plan assumes sm_count / 2 pairs resident at
  * once; launches on a device use the number of pairs that fit on it
  * (clusters are placed within GPCs), which i4g_max_pairs reports for the
  * current device. WHOLE schedules report the grid in CTAs. */
