@@ -99,7 +99,10 @@ struct Cfg {
   static constexpr int ACT_BYTES = ROWS * BK * 2;
   static constexpr int A_STAGES = SS ? 6 : (TILE_M <= 128 ? 8 : 5);
   static constexpr int W_ST = SS ? 8 : W_STAGES;               // packed weight stages
-  static constexpr int T_ST = SS ? 4 : T_STAGES;               // dequantised weight stages
+  // dequantised weight stages; single CTAs: one per activation stage, the
+  // two sharing one pair of barriers (one wait and one commit per block for
+  // the MMA thread)
+  static constexpr int T_ST = SS ? 4 : A_STAGES;
   static constexpr int DEQ_BYTES = TILE_N * BK * 2;            // one smem weight tile (SS)
   static constexpr int ACT_OFF = 0;
   static constexpr int DEQ_OFF = ACT_OFF + A_STAGES * ACT_BYTES;
@@ -112,6 +115,7 @@ struct Cfg {
   static_assert(ACT_BYTES % 1024 == 0, "activation stage must keep 1024B alignment");
   static_assert(DEQ_BYTES % 1024 == 0, "weight tile must keep 1024B alignment");
   static_assert(ACC_COL + ACC * TILE_M <= TMEM_COLS, "TMEM budget");
+  static_assert(SS || T_ST * T_COLS <= ACC_COL, "TMEM weight stages below the accumulators");
   static_assert(DYN_BYTES <= 232448, "shared memory budget");
   static_assert(T_ST % DEQ_GROUPS == 0 && W_ST % DEQ_GROUPS == 0, "stage ownership");
 };
@@ -484,9 +488,14 @@ __global__ void __launch_bounds__(THREADS, 1)
   auto aempty = [&](int i) { return bar_base + 8u * (A_STAGES + i); };
   auto wfull = [&](int i) { return bar_base + 8u * (2 * A_STAGES + i); };
   auto wempty = [&](int i) { return bar_base + 8u * (2 * A_STAGES + W_STAGES + i); };
-  auto tfull = [&](int i) { return bar_base + 8u * (2 * A_STAGES + 2 * W_STAGES + i); };
+  // single CTAs: a block's activation stage and TMEM weight stage share
+  // afull (TMA bytes + every dequant thread) and aempty (MMA completion)
+  constexpr bool UNI = !(CG == 2);
+  auto tfull = [&](int i) {
+    return UNI ? afull(i) : bar_base + 8u * (2 * A_STAGES + 2 * W_STAGES + i);
+  };
   auto tempty = [&](int i) {
-    return bar_base + 8u * (2 * A_STAGES + 2 * W_STAGES + T_STAGES + i);
+    return UNI ? aempty(i) : bar_base + 8u * (2 * A_STAGES + 2 * W_STAGES + T_STAGES + i);
   };
   auto dfull = [&](int i) {
     return bar_base + 8u * (2 * A_STAGES + 2 * W_STAGES + 2 * T_STAGES + i);
@@ -526,18 +535,19 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int i = 0; i < A_STAGES; ++i) {
       // own producer's expected bytes; in the even CTA of a pair also the odd
       // CTA's relay (its half landed)
-      mbar_init(afull(i), PAIR && leader ? 2 : 1);
+      // single CTAs: also every dequant thread (the TMEM stage of the block)
+      mbar_init(afull(i), PAIR ? (leader ? 2 : 1) : 1 + 4 * 32);
       mbar_init(aempty(i), 1);  // MMA completion
     }
     for (int i = 0; i < W_STAGES; ++i) {
       mbar_init(wfull(i), 1);
       mbar_init(wempty(i), 4);  // the four warps of the dequant group that read it
     }
-    for (int i = 0; i < T_STAGES; ++i) {
-      // single CTAs: every dequant thread (TMEM stores); pairs: one arrival
-      // per local dequant warp, and in the even CTA also the odd CTA's relay
-      mbar_init(tfull(i), PAIR ? (leader ? 4 + 1 : 4) : 4 * 32);
-      mbar_init(tempty(i), 1);           // MMA completion
+    for (int i = 0; !UNI && i < T_STAGES; ++i) {
+      // pairs: one arrival per local dequant warp, and in the even CTA also
+      // the odd CTA's relay
+      mbar_init(tfull(i), leader ? 4 + 1 : 4);
+      mbar_init(tempty(i), 1);  // MMA completion
     }
     for (int i = 0; i < ACC; ++i) {
       mbar_init(dfull(i), 1);
@@ -675,7 +685,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t ph = (it / A_STAGES) & 1u;
           const int ts = it % T_STAGES;
           const uint32_t tph = (it / T_STAGES) & 1u;
-          if (!wait_in(afull(s), ph) || !wait_in(tfull(ts), tph)) {
+          if (!wait_in(afull(s), ph) || (!UNI && !wait_in(tfull(ts), tph))) {
             ok = false;
             break;
           }
@@ -695,7 +705,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
           }
           commit(aempty(s));
-          commit(tempty(ts));
+          if constexpr (!UNI) commit(tempty(ts));
         }
         if (!ok) break;
         commit(dfull(acc));
