@@ -144,8 +144,10 @@ int i4g_gemm_variant(const void* A, const uint8_t* tiles, const void* scales,
 /* The tcgen05 kernel runs ceil(M/TILE_M) x N/128 output tiles on one CTA per
  * SM. When the tile count is not a multiple of the SM count, the *_ws entry
  * points share the tiles of the last, partial wave out along K over all SMs
- * (stream-K: equal shares of the leftover tiles' 64-k blocks, one per CTA;
- * or, with a smaller workspace, each leftover tile split 2 to 4 ways) and
+ * (each leftover tile split 2 to 4 ways; with the I4G_STREAMK=1 environment
+ * variable, read at the first launch, stream-K where it is cheaper: equal
+ * shares of the leftover tiles' 64-k blocks, one per CTA; opt-in because it
+ * gave an intermittently wrong tile on B200, a race not yet found) and
  * reduce the FP32 partial tiles through a caller-owned workspace, in a fixed
  * order, so results are bitwise reproducible and within the usual FP32
  * accumulation tolerance of the unsplit kernel. The decode kernel (M <= 16,

@@ -7,6 +7,8 @@ choose_cluster and sk_plan, and expected_decode_schedule its pick_schedule
 and slice_grid (csrc/gemm_decode.cu); expected_workspace is what
 i4g_gemm_workspace_size reports.
 """
+import os
+
 import torch
 
 TICKET_BYTES = 4096  # arrival counters at the start of every workspace
@@ -27,9 +29,13 @@ def device_pairs():
 def plan_cg(tile_m, N):
     """CTAs per tile: 2 (a CTA pair) for 256-row tiles of N % 256 == 0 when
     I4G_PAIR=1 is set, else 1."""
-    import os
     pairs_on = os.environ.get("I4G_PAIR", "0") not in ("", "0")
     return 2 if pairs_on and tile_m == 256 and N % 256 == 0 else 1
+
+
+def streamk_on():
+    """The tcgen05 stream-K tail runs only with I4G_STREAMK=1 (opt-in)."""
+    return os.environ.get("I4G_STREAMK", "0") not in ("", "0")
 
 
 def expected_plan(M, N, K, budget=1 << 62, sms=None, pairs=None):
@@ -57,7 +63,7 @@ def expected_plan(M, N, K, budget=1 << 62, sms=None, pairs=None):
         best, plan = (waves + 1.0 / f) * t_tile + 12.0, (f"split{f}", need, tile_m)
     run = rem * kb
     chunks = min(units, 3 * rem, run // 8)
-    if chunks > rem and cg == 1:
+    if chunks > rem and cg == 1 and streamk_on():
         most = max((((t + 1) * kb) * chunks - 1) // run - ((t * kb + 1) * chunks - 1) // run + 1
                    for t in range(rem))
         need = TICKET_BYTES + (rem + chunks - 1) * tile_bytes

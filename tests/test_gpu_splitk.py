@@ -1,7 +1,7 @@
 """Split-K schedules of the tcgen05 kernel (the *_ws entry points).
 
-The tiles of the last, partial wave are shared out along K (stream-K shares
-over all SMs, or equal splits when the workspace is smaller) and reduced
+The tiles of the last, partial wave are shared out along K (equal splits;
+stream-K shares over all SMs with I4G_STREAMK=1) and reduced
 through a caller-owned FP32 workspace in a fixed order. Results are checked
 against the oracle under the same tolerance as the unsplit kernel
 (tests/parity.py), are bitwise reproducible, and leave the workspace counters
@@ -13,7 +13,7 @@ import torch
 
 import oracle
 from parity import assert_gemm_parity, fp32_report, gemm_report, make_inputs, oracle_case, u16
-from plans import TICKET_BYTES, expected_plan, expected_workspace
+from plans import TICKET_BYTES, expected_plan, expected_workspace, streamk_on
 
 pytestmark = pytest.mark.gpu
 
@@ -147,12 +147,16 @@ def test_misaligned_workspace_rejected(i4g):
 @pytest.mark.parametrize("M,N,K,grp", [(1024, 7168, 8192, 64), (2048, 3968, 12288, 32),
                                        (1024, 3200, 12288, 128)])
 def test_stream_k_tail_parity(i4g, M, N, K, grp):
-    """Stream-K shares over all SMs (after whole waves, or as the only wave),
-    up to three or four partial tiles per output tile; sampled rows cover the
-    tail tiles' row blocks."""
-    assert expected_plan(M, N, K)[0] == "stream-k"
+    """The shapes the stream-K tail serves when it is enabled (I4G_STREAMK=1:
+    shares over all SMs after whole waves, or as the only wave, up to three
+    or four partial tiles per output tile); by default they run equal splits
+    or whole tiles. Either way: parity on sampled rows covering the tail
+    tiles' row blocks, and a second launch on the same workspace equal bit
+    for bit."""
+    kind = expected_plan(M, N, K)[0]
+    assert (kind == "stream-k") == streamk_on(), kind
     rep, c, (a, lin, ws) = split_case(i4g, M, N, K, grp, rows=sample_rows(M, K))
-    print("stream-k", M, N, K, grp, rep)
+    print(kind, M, N, K, grp, rep)
     assert_gemm_parity(rep)
     c2 = torch.empty_like(c)
     i4g.launch_final_ws(a, lin.tiles, lin.scales, c2, M, N, K, grp, ws)

@@ -57,7 +57,7 @@ def _check_two_calls(i4g, L, ad, lin, ref, M, N, K, grp):
 @pytest.mark.parametrize("M,N,K,grp", [
     (4096, 4096, 4096, 128),   # tcgen05, two-way split of the last wave
     (512, 1024, 4096, 64),     # tcgen05, four-way split
-    (1024, 7168, 8192, 64),    # tcgen05, stream-K tail
+    (1024, 7168, 8192, 64),    # tcgen05, split tail (stream-K with I4G_STREAMK=1)
     (300, 640, 2048, 32),      # tcgen05, ragged M
     (8, 4096, 4096, 128),      # decode, cluster schedule (no scratch)
     (1, 28672, 8192, 128),     # decode, stream-K schedule through the scratch
