@@ -92,30 +92,40 @@ class ClockSampler:
         self.first = 0
         self.stop = threading.Event()
 
-    def _nvml_poll(self):
+    def _nvml_sample(self):
         n = self.nvml
-        h = n.nvmlDeviceGetHandleByIndex(self.device_index)
-        mx = n.nvmlDeviceGetMaxClockInfo(h, n.NVML_CLOCK_SM)
-        bits = {"hw_slowdown": n.nvmlClocksEventReasonHwSlowdown,
-                "hw_thermal_slowdown": n.nvmlClocksEventReasonHwThermalSlowdown,
-                "sw_thermal_slowdown": n.nvmlClocksEventReasonSwThermalSlowdown,
-                "sw_power_cap": n.nvmlClocksEventReasonSwPowerCap}
+        try:
+            sm = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
+            r = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+            self.samples.append((sm, self.max_mhz, {k for k, b in self.bits.items() if r & b}))
+        except Exception:  # noqa: BLE001 - a failed read only loses a sample
+            pass
+
+    def _nvml_poll(self):
         while not self.stop.is_set():
-            try:
-                sm = n.nvmlDeviceGetClockInfo(h, n.NVML_CLOCK_SM)
-                r = n.nvmlDeviceGetCurrentClocksEventReasons(h)
-                self.samples.append((sm, mx, {k for k, b in bits.items() if r & b}))
-            except Exception:  # noqa: BLE001 - a failed read only loses a sample
-                pass
+            self._nvml_sample()
             self.stop.wait(self.period_s)
 
     def __enter__(self):
         try:
             import pynvml
             pynvml.nvmlInit()
-            self.nvml = pynvml
+            self.nvml = n = pynvml
+            self.handle = n.nvmlDeviceGetHandleByIndex(self.device_index)
+            self.max_mhz = n.nvmlDeviceGetMaxClockInfo(self.handle, n.NVML_CLOCK_SM)
+            self.bits = {"hw_slowdown": n.nvmlClocksEventReasonHwSlowdown,
+                         "hw_thermal_slowdown": n.nvmlClocksEventReasonHwThermalSlowdown,
+                         "sw_thermal_slowdown": n.nvmlClocksEventReasonSwThermalSlowdown,
+                         "sw_power_cap": n.nvmlClocksEventReasonSwPowerCap}
             self.thread = threading.Thread(target=self._nvml_poll, daemon=True)
             self.thread.start()
+            # the poller is running before the timed region starts; samples
+            # from here on are the region's (a short region still gets some:
+            # the poller runs while the host waits in the final synchronize)
+            t0 = time.time()
+            while not self.samples and time.time() - t0 < 2.0:
+                time.sleep(0.0005)
+            self.first = len(self.samples)
             return self
         except Exception:  # noqa: BLE001 - fall back to nvidia-smi
             self.nvml = None
@@ -140,6 +150,7 @@ class ClockSampler:
 
     def __exit__(self, *exc):
         if self.nvml is not None:
+            self._nvml_sample()  # as the region ends
             self.stop.set()
             self.thread.join(timeout=5)
             try:
@@ -157,7 +168,7 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], None, set()
         if self.nvml is not None:
-            for s_mhz, m_mhz, rs in self.samples:
+            for s_mhz, m_mhz, rs in self.samples[self.first:]:
                 sm.append(float(s_mhz))
                 mx = float(m_mhz)
                 reasons |= rs
