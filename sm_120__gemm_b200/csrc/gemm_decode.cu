@@ -45,6 +45,7 @@ constexpr int CWARPS = NCOL / 16;
 constexpr int THREADS = (CWARPS + 1) * 32;
 constexpr int CTAS_PER_SM = 2;
 constexpr int SMEM_PER_SM = 227 * 1024;
+constexpr int kDefaultPrefetchBlocks = 8;
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -351,7 +352,7 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM)
     decode_kernel(const __grid_constant__ CUtensorMap act_map,
                   const uint8_t* __restrict__ tiles, const __half* __restrict__ scales,
                   const __grid_constant__ Outputs out, int M, int N, int K, int* status,
-                  unsigned long long wait_limit_ns) {
+                  unsigned long long wait_limit_ns, int prefetch_blocks) {
   using L = Layout<MT, GROUP, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -385,10 +386,37 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM)
   }
   __syncthreads();
 
+  // Launched as a programmatic dependent of the previous kernel on the stream,
+  // this CTA may start while that kernel still runs. Until the dependency
+  // wait it touches only its own shared memory and warms L2 with the first
+  // `prefetch_blocks` blocks of its weight slice and their scales (a prefetch
+  // never stales: see bulk_prefetch_l2), so the previous kernel's tail
+  // overlaps this kernel's first HBM reads. A, the weights and C are read
+  // and written only after the wait. The prefetch is kept short (two ring
+  // stages by default): the copy unit serves it before the ring's first
+  // copies, so a long one delays the fill when nothing runs before the kernel
+  // (measured on B200 at K = 4096, N = 14336, M = 1: 12.1 us per call without
+  // prefetch, 12.2 with 8 blocks, 14.6 with 64).
+  if (warp == CWARPS && lane == 0) {
+    prefetch_tensormap(&act_map);
+    const int nkb = min(kb1 - kb0, prefetch_blocks);
+    if (nkb > 0) {
+      const uint8_t* wsrc = tiles + (static_cast<size_t>(nt) * kblocks + kb0) * 4096;
+      const uint32_t wbytes = static_cast<uint32_t>(nkb) * 4096u;
+      for (uint32_t off = 0; off < wbytes; off += 65536u)
+        bulk_prefetch_l2(wsrc + off, min(65536u, wbytes - off));
+      const int g0 = kb0 * BK / GROUP;
+      const int g1 = ((kb0 + nkb) * BK + GROUP - 1) / GROUP;
+      bulk_prefetch_l2(scales + (static_cast<size_t>(nt) * groups + g0) * 128,
+                       static_cast<uint32_t>(g1 - g0) * 256u);
+    }
+  }
+  grid_dependency_wait();
+  if (threadIdx.x == 0) launch_dependents();
+
   if (warp == CWARPS) {
     // --------------------------------------------------------------- producer
     if (lane == 0) {
-      prefetch_tensormap(&act_map);
       int issued = 0;
       for (int i = 0; i < nstages; ++i) {
         const int s = i % STAGES;
@@ -932,6 +960,17 @@ __global__ void __launch_bounds__(SL_THREADS, 1)
   }
 }
 
+// 64-k blocks of its weight slice a cluster-schedule CTA warms L2 with
+// before its dependency wait (I4G_DECODE_PREFETCH overrides; read once).
+int prefetch_blocks() {
+  static const int v = [] {
+    const char* e = std::getenv("I4G_DECODE_PREFETCH");
+    const int b = e ? std::atoi(e) : kDefaultPrefetchBlocks;
+    return b < 0 ? 0 : b;
+  }();
+  return v;
+}
+
 template <int MT, int GROUP>
 cudaError_t launch_typed(const CUtensorMap& act_map, const uint8_t* tiles, const __half* scales,
                          const Outputs& out, int M, int N, int K, int cluster, int* status,
@@ -947,15 +986,17 @@ cudaError_t launch_typed(const CUtensorMap& act_map, const uint8_t* tiles, const
   cfg.blockDim = dim3(THREADS);
   cfg.dynamicSmemBytes = L::DYN;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = cluster;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, kernel, act_map, tiles, scales, out, M, N, K, status,
-                            wait_limit_ns);
+                            wait_limit_ns, prefetch_blocks());
 }
 
 template <int MT, int GROUP>

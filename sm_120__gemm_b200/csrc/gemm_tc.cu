@@ -576,6 +576,13 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  // Launched as a programmatic dependent of the previous kernel on the stream,
+  // this CTA may set up (barriers, TMEM, descriptor prefetch) while that
+  // kernel's last CTAs still run; A, the weights, C and the split-K workspace
+  // are touched only after the dependency wait.
+  grid_dependency_wait();
+  if (threadIdx.x == 0) launch_dependents();
+
   if (warp == 0) {
     // ------------------------------------------------- activation producer
     if (lane == 0) {
@@ -1197,13 +1204,22 @@ cudaError_t launch_impl(const CUtensorMap& act_map, const uint8_t* tiles, const 
   cfg.blockDim = dim3(THREADS);
   cfg.dynamicSmemBytes = L::DYN_BYTES;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = CG;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (CG > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = CG;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = CG > 1 ? 1 : 0;
+  cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, kernel, act_map, tiles, scales, out, M, N, K, plan.sched,
                             tickets, partials, status, wait_limit_ns);
 }

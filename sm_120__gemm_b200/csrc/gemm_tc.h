@@ -5,6 +5,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <atomic>
+#include <cstdlib>
 #include <cstdint>
 
 namespace i4g {
@@ -24,6 +25,17 @@ cudaError_t ensure_dynamic_smem(Kernel kernel, int bytes, std::atomic<uint64_t>&
   e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_release);
   return e;
+}
+
+// The GEMM kernels are launched as programmatic dependents of the kernel
+// before them on the stream (they may start while it runs, and wait for it
+// before touching A, C or a workspace), unless I4G_PDL=0 (read once).
+inline bool pdl_enabled() {
+  static const bool v = [] {
+    const char* e = std::getenv("I4G_PDL");
+    return !(e && e[0] == '0' && e[1] == 0);
+  }();
+  return v;
 }
 
 // Where a launch writes C: `count` copies (this GPU's, then peers' through

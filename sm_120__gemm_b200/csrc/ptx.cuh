@@ -229,6 +229,28 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
       : "memory");
 }
 
+// Warms L2 with a contiguous global range (16-byte aligned, size % 16 == 0).
+// Nothing lands in shared memory, so the range may still be written by an
+// earlier kernel: L2 is the point of coherence and later loads see the writes.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// ------------------------------------------- programmatic dependent launch
+
+// Waits until every grid this one depends on programmatically has completed
+// and its memory operations are visible; returns at once when the grid was
+// launched without a programmatic dependency.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Lets a programmatically dependent grid be scheduled once every CTA of this
+// grid has issued this (or exited); a no-op without such a dependent.
+__device__ __forceinline__ void launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ------------------------------------------------------ clusters / CTA pairs
 
 __device__ __forceinline__ uint32_t cluster_rank() {
