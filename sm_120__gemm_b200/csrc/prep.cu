@@ -323,7 +323,7 @@ __global__ void __launch_bounds__(THREADS)
   constexpr int GPC = KC / GROUP;           // groups per slab
   constexpr int P = THREADS / (64 * GPC);   // threads per (group, column pair)
   constexpr int RPP = GROUP / P;            // rows each of them scans
-  static_assert(P >= 1 && (P & (P - 1)) == 0 && RPP >= 1, "scale pass split");
+  static_assert(P >= 1 && (P & (P - 1)) == 0 && RPP % 8 == 0, "scale pass split");
   __shared__ __align__(16) __half slab[KC * 128];
   __shared__ float sf[GPC][128];  // scales
   __shared__ float sr[GPC][128];  // their rounded reciprocals; NaN: not a normal scale
@@ -331,9 +331,6 @@ __global__ void __launch_bounds__(THREADS)
   const int kc = blockIdx.y;
   const int k0 = kc * KC;
   auto chunk_at = [](int row, int ch) { return row * 128 + ((ch ^ (2 * ((row >> 3) & 3))) << 3); };
-  auto pair_at = [&](int row, int np) -> __half2 {
-    return *reinterpret_cast<const __half2*>(&slab[chunk_at(row, np >> 2) + 2 * (np & 3)]);
-  };
   // B rows k0..k0+KC, columns 128 nt..: 16 chunks of 16 bytes per row
 #pragma unroll
   for (int j = 0; j < KC * 16 / THREADS; ++j) {
@@ -348,14 +345,22 @@ __global__ void __launch_bounds__(THREADS)
   {
     // group abs-max of a column pair over RPP rows per thread, combined over
     // the P adjacent lanes of the pair (the maximum ignores NaN, as the
-    // reference's std::max-style update does)
+    // reference's std::max-style update does). Lane `part` takes the group's
+    // 8-row runs part, part + P, ...: the eight rows of a run share one chunk
+    // swizzle (one base address, then a 128-half row stride), and the P lanes
+    // of a pair read runs with different swizzles, i.e. different banks.
     const int part = threadIdx.x % P;
     const int np = (threadIdx.x / P) % 64;
     const int gl = threadIdx.x / (P * 64);
     __half2 m = __float2half2_rn(0.0f);
-    const int r0 = gl * GROUP + part * RPP;
-#pragma unroll 8
-    for (int r = r0; r < r0 + RPP; ++r) m = __hmax2(m, __habs2(pair_at(r, np)));
+#pragma unroll
+    for (int q = 0; q < RPP / 8; ++q) {
+      const int r8 = gl * GROUP + (q * P + part) * 8;
+      const __half2* xp =
+          reinterpret_cast<const __half2*>(&slab[chunk_at(r8, np >> 2) + 2 * (np & 3)]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) m = __hmax2(m, __habs2(xp[e * 64]));
+    }
 #pragma unroll
     for (int o = 1; o < P; o <<= 1) m = __hmax2(m, __shfl_xor_sync(0xffffffffu, m, o));
     const float2 vmax = __half22float2(m);
