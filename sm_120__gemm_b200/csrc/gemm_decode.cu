@@ -524,7 +524,7 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM)
                      const uint8_t* __restrict__ tiles, const __half* __restrict__ scales,
                      const __grid_constant__ Outputs out, int M, int N, int K,
                      uint32_t* __restrict__ tickets, float4* __restrict__ partials, int* status,
-                     unsigned long long wait_limit_ns) {
+                     unsigned long long wait_limit_ns, int prefetch_blocks) {
   using L = Layout<MT, GROUP, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -557,10 +557,24 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM)
   }
   __syncthreads();
 
+  // Programmatic dependent launch, as in decode_kernel: before the wait only
+  // shared memory and an L2 warm-up of the run's first weight blocks; A, the
+  // weights, C and the workspace (tickets, partials) after it.
+  if (warp == CWARPS && lane == 0) {
+    prefetch_tensormap(&act_map);
+    const int nt = static_cast<int>(u0 / kblocks), kb = static_cast<int>(u0 % kblocks);
+    const int nkb = static_cast<int>(
+        min(static_cast<long>(min(kblocks - kb, prefetch_blocks)), u1 - u0));
+    if (nkb > 0)
+      bulk_prefetch_l2(tiles + (static_cast<size_t>(nt) * kblocks + kb) * 4096,
+                       static_cast<uint32_t>(nkb) * 4096u);
+  }
+  grid_dependency_wait();
+  if (threadIdx.x == 0) launch_dependents();
+
   if (warp == CWARPS) {
     // --------------------------------------------------------------- producer
     if (lane == 0) {
-      prefetch_tensormap(&act_map);
       int i = 0, issued = 0;
       bool ok = true;
       for (long u = u0; ok && u < u1;) {
@@ -1013,9 +1027,18 @@ cudaError_t launch_sk_typed(const CUtensorMap& act_map, const uint8_t* tiles,
   uint32_t* tickets = static_cast<uint32_t*>(workspace);
   float4* partials =
       reinterpret_cast<float4*>(static_cast<char*>(workspace) + tc::kTicketBytes);
-  kernel<<<grid, THREADS, L::DYN, stream>>>(act_map, tiles, scales, out, M, N, K, tickets,
-                                            partials, status, wait_limit_ns);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = L::DYN;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, act_map, tiles, scales, out, M, N, K, tickets,
+                            partials, status, wait_limit_ns, prefetch_blocks());
 }
 
 // Tuning override for the cluster size (1-8), read once from
