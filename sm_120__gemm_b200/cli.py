@@ -331,7 +331,11 @@ def configs(iters, csv_path=""):
     l2 = torch.cuda.get_device_properties(0).L2_cache_size
     lines = ["config,M,N,K,group,kernel,schedule,us_per_call,tflops,algorithmic_gbs,"
              "frac_tensor,frac_hbm"]
+    import time
     for (label, M, N, K, g) in config_shapes():
+        # let clocks and power recover from the previous row (the prefill
+        # rows run the GPU at its power cap for a third of a second)
+        time.sleep(1.0)
         wbytes = K * N // 2
         nw = max(1, min(8, -(-2 * l2 // wbytes)))
         na = max(1, min(4, -(-2 * l2 // (2 * M * K))))

@@ -1010,8 +1010,10 @@ cudaError_t launch_typed(const CUtensorMap& act_map, const uint8_t* tiles, const
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 2 : 1;
+  // the L2 warm-up only pays when it overlaps the previous kernel (without
+  // PDL, K = 8192, N = 7168, g64, M = 16: 13.7 us with it, 13.1 without)
   return cudaLaunchKernelEx(&cfg, kernel, act_map, tiles, scales, out, M, N, K, status,
-                            wait_limit_ns, prefetch_blocks());
+                            wait_limit_ns, pdl ? prefetch_blocks() : 0);
 }
 
 template <int MT, int GROUP>
@@ -1039,7 +1041,8 @@ cudaError_t launch_sk_typed(const CUtensorMap& act_map, const uint8_t* tiles,
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, act_map, tiles, scales, out, M, N, K, tickets,
-                            partials, status, wait_limit_ns, prefetch_blocks());
+                            partials, status, wait_limit_ns,
+                            pdl_enabled() ? prefetch_blocks() : 0);
 }
 
 // Tuning override for the cluster size (1-8), read once from
