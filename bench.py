@@ -311,7 +311,7 @@ def run_ours(args, rank, world, local_rank):
     # against an NCCL all-gather of per-rank plain GEMMs (outside the timing).
     gather_check = None
     if gather != "none":
-        last = args.warmup + args.steps - 1
+        last = args.warmup + args.steps + split_steps - 1  # the per-GEMM pass ran last
         g = GROUPS[-1]
         lin = lins[g][(last + len(GROUPS) - 1) % n_wset]
         a = acts[(3 * last + len(GROUPS) - 1) % n_act]
@@ -390,10 +390,10 @@ def run_ours(args, rank, world, local_rank):
 
 def _time_max(fn, iters, dev, world):
     """Device time per call of fn (CUDA events on the current stream, after 3
-    warm-ups), max over ranks. The stream first runs a 2 ms spin kernel while
-    the host enqueues every call, and the start event follows the spin: the
-    calls then run back to back on the device, so a call shorter than its
-    Python launch path (decode-sized M) is timed, not the host."""
+    warm-ups), max over ranks. On one GPU the stream first runs a 2 ms spin
+    kernel while the host enqueues every call, and the start event follows the
+    spin: the calls then run back to back on the device, so a call shorter
+    than its Python launch path (decode-sized M) is timed, not the host."""
     import torch
     import torch.distributed as dist
     for _ in range(3):
@@ -401,8 +401,11 @@ def _time_max(fn, iters, dev, world):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    clock_khz = getattr(torch.cuda.get_device_properties(dev), "clock_rate", 0) or 1965000
-    torch.cuda._sleep(int(2e-3 * clock_khz * 1e3))
+    if world == 1:
+        # (with several ranks the spin would move the ranks' host skew into
+        # the first call's cross-GPU barrier, so they start unqueued)
+        clock_khz = getattr(torch.cuda.get_device_properties(dev), "clock_rate", 0) or 1965000
+        torch.cuda._sleep(int(2e-3 * clock_khz * 1e3))
     b, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     b.record()
     for _ in range(iters):
