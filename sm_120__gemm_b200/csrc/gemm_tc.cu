@@ -74,7 +74,8 @@ constexpr int NUM_EPI_WARPS = 16;   // four per TMEM lane quarter
 constexpr int FIRST_DEQ_WARP = 3;
 constexpr int FIRST_EPI_WARP = FIRST_DEQ_WARP + NUM_DEQ_WARPS;
 constexpr int THREADS = 32 * (FIRST_EPI_WARP + NUM_EPI_WARPS);
-// 23 warps (736 threads): 88 registers a thread
+// 23 warps (736 threads): 80 registers a thread (six warps share one SMSP's
+// 16,384 registers)
 static_assert(NUM_DEQ_WARPS == 4 && NUM_EPI_WARPS == 16, "each TMEM lane quarter (warp % 4) "
               "has one dequant warp and four epilogue warps");
 constexpr int TMEM_COLS = 512;
